@@ -1,0 +1,120 @@
+/*
+ * Batched B200 entry points of the token sampler (libnoel_sampler_cuda.so).
+ *
+ * The reference samples one host row per call (Sain-Kai/noel
+ * src/sampler.c:80, called from src/engine.c:387).  These entry points run
+ * the same computation for a batch of rows resident on the GPU: per row the
+ * repetition penalty over its history, temperature, top-k, top-p and one
+ * draw from the row's own xorshift128+ state, with results identical to the
+ * reference's for the same row, history, config and state.  They have no
+ * counterpart in the reference beyond that per-row function; each cites the
+ * reference lines whose semantics it carries.
+ *
+ * Conventions: plain pointers and sizes; "d_" pointers are device memory of
+ * the current device; stream is a cudaStream_t (NULL = default stream).
+ * Every function returns NOEL_OK (0) or a negative status; the calling
+ * thread's last status and message are kept for noel_sampler_cuda_last_error().
+ */
+#ifndef NOEL_SAMPLER_CUDA_H
+#define NOEL_SAMPLER_CUDA_H
+
+#include "sampler.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    NOEL_OK = 0,
+    NOEL_ERR_INVALID_ARG = -1,   /* NULL pointer, bad size or misaligned row */
+    NOEL_ERR_CUDA = -2,          /* a CUDA runtime call failed */
+    NOEL_ERR_NO_DEVICE = -3,     /* no usable sm_100 device */
+    NOEL_ERR_TOO_LARGE = -4,     /* size beyond what the entry point supports */
+    NOEL_ERR_UNSUPPORTED = -5,   /* option combination not supported */
+};
+
+enum { NOEL_DTYPE_F32 = 0, NOEL_DTYPE_BF16 = 1 };
+
+/* Per-row statistics (out_stats, 4 x int32 per row). */
+enum {
+    NOEL_STAT_NUM_CANDS = 0,  /* candidates with diff > -15, or -1 if > the kept set */
+    NOEL_STAT_N_TOPK = 1,     /* list length after top-k (sampler.c:155-157) */
+    NOEL_STAT_N_FINAL = 2,    /* list length after top-p (sampler.c:165-179) */
+    NOEL_STAT_FLAGS = 3,      /* NOEL_ROW_* bits */
+};
+enum {
+    NOEL_ROW_GREEDY = 1,      /* argmax branch, no RNG step (sampler.c:106-116) */
+    NOEL_ROW_EXACT_PASS = 2,  /* finished by the two-pass exact kernel */
+    NOEL_ROW_FALLBACK = 4,    /* no candidate: {0, 1.0} (sampler.c:145-149) */
+};
+
+/* Optional outputs and options of one batched call. */
+typedef struct {
+    float *d_probs;           /* [B] val(chosen)/mass, or NULL (1.0 for greedy) */
+    int32_t *d_list_ids;      /* [B][list_len] drawn-from list, sorted, -1 padded, or NULL */
+    float *d_list_probs;      /* [B][list_len] their probabilities, or NULL */
+    int list_len;
+    int list_weights;         /* 1: d_list_probs gets the unnormalised weights (sampler.c:140) */
+    int32_t *d_stats;         /* [B][4] NOEL_STAT_* per row, or NULL */
+    int write_back;           /* 1: store penalised values into the fp32 logits (sampler.c:96-100) */
+} noel_sample_extras_t;
+
+/*
+ * Sample B rows on the device.  Replaces B calls of noel_sampler_sample
+ * (sampler.c:80-192) with one launch sequence.
+ *   d_logits   [B][ld] fp32 or bf16 (dtype), row b at d_logits + b*ld elements;
+ *              ld >= vocab; the base must be aligned to the element size.
+ *   d_history  [B][hld] int32 token ids or NULL; the first history_len are used
+ *              (window per cfg->repetition_window, sampler.c:89-90).
+ *   d_rng      [B][2] xorshift128+ states, advanced once per non-greedy row.
+ *   d_ids      [B] sampled ids.
+ *   d_probs    [B] probability of the sampled id, or NULL.
+ */
+int noel_sampler_sample_batch(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
+                              int batch, int vocab, size_t ld, const int32_t *d_history,
+                              int history_len, size_t hld, uint64_t *d_rng, int32_t *d_ids,
+                              float *d_probs, void *stream);
+
+/* As noel_sampler_sample_batch, with the optional outputs of extras (may be NULL). */
+int noel_sampler_sample_batch_ex(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
+                                 int batch, int vocab, size_t ld, const int32_t *d_history,
+                                 int history_len, size_t hld, uint64_t *d_rng, int32_t *d_ids,
+                                 const noel_sample_extras_t *extras, void *stream);
+
+/*
+ * Host-buffer form of noel_sampler_sample_batch for callers whose logits are
+ * in host memory (the reference engine's layout, src/engine.c:59): copies the
+ * rows, histories and states to the device, samples, and copies ids, states
+ * and (if h_probs) probabilities back; synchronous.  Pinned host memory gives
+ * the fastest copies.  logits rows are h_logits + b*ld fp32 or bf16 elements.
+ */
+int noel_sampler_sample_batch_host(const noel_sampler_config_t *cfg, const void *h_logits, int dtype,
+                                   int batch, int vocab, size_t ld, const int32_t *h_history,
+                                   int history_len, size_t hld, uint64_t *h_rng, int32_t *h_ids,
+                                   float *h_probs);
+
+/* Calling thread's last status (NOEL_OK after a successful call). */
+int noel_sampler_cuda_last_error(void);
+/* Calling thread's last error message ("" if none). */
+const char *noel_sampler_cuda_last_error_message(void);
+/* Static name of a status code. */
+const char *noel_sampler_cuda_status_string(int status);
+
+/* Number of inputs x in (-15, 0] whose exp weight comes from the C-library
+ * table rather than the correctly rounded exp (diagnostic). */
+int noel_sampler_cuda_expf_table_size(void);
+
+/*
+ * Checksum of the device's exp weight bits over every float in (-15, 0]
+ * (bit patterns 0x80000000 .. 0xC1700000), in chunks of 2^chunk_log2 inputs:
+ * out[c] = sum over the chunk of mix64((x_bits << 32) | weight_bits).  The
+ * same sums over the C library's expf pin the device weights to it.
+ * d_out has room for ceil(0x41700000 / 2^chunk_log2) uint64 values.
+ */
+int noel_sampler_cuda_expf_checksums(int chunk_log2, uint64_t *d_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NOEL_SAMPLER_CUDA_H */

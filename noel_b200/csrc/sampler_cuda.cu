@@ -1,0 +1,596 @@
+/*
+ * Host side of libnoel_sampler_cuda.so: the reference's sampler ABI
+ * (include/sampler.h) and the batched entry points (include/noel_sampler_cuda.h).
+ *
+ * Device state never lives in noel_sampler_t (callers embed it by value and
+ * poke its fields, Sain-Kai/noel src/main.c:259-262): it is kept per device in
+ * a process-global context, the way the reference keeps its CUDA context in
+ * a global (src/cuda_backend.c:8), plus per-thread staging buffers and stream
+ * for the single-row ABI.  There is no CPU fallback: a missing or
+ * unsupported device is an error.
+ */
+#include <cuda_runtime.h>
+
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "noel_sampler_cuda.h"
+#include "sampler_kernels.cuh"
+
+#define NOEL_EXPF_QUAL static __device__ const
+#include "_gen/expf_table.inc"
+
+using namespace noel;
+
+namespace {
+
+/* ------------------------------------------------------------------ errors */
+thread_local int t_status = NOEL_OK;
+thread_local char t_msg[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+    t_status = code;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_msg, sizeof(t_msg), fmt, ap);
+    va_end(ap);
+    return code;
+}
+int ok() {
+    t_status = NOEL_OK;
+    t_msg[0] = '\0';
+    return NOEL_OK;
+}
+
+#define CUDA_TRY(call)                                                                     \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess) return fail(NOEL_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+/* -------------------------------------------------------- device context */
+struct Workspace {
+    int32_t *counters = nullptr;  // 4 ints
+    int32_t *rows = nullptr;      // row list of the exact kernel
+    uint2 *slots = nullptr;       // nslots x 2 x vocab
+    int rows_cap = 0, vocab_cap = 0, nslots = 0;
+};
+
+struct DeviceCtx {
+    bool ready = false;
+    int sms = 0;
+    size_t smem_optin = 0;
+    ExpTable et{};
+    std::map<cudaStream_t, Workspace> ws;
+    std::map<const void *, size_t> smem_set;  // kernel -> dynamic smem attribute set
+};
+
+std::mutex g_mu;
+std::vector<DeviceCtx> g_dev;
+
+int device_ctx(DeviceCtx **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(NOEL_ERR_NO_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+    std::lock_guard<std::mutex> lk(g_mu);
+    if ((int)g_dev.size() <= dev) g_dev.resize(dev + 1);
+    DeviceCtx &c = g_dev[dev];
+    if (!c.ready) {
+        cudaDeviceProp p;
+        CUDA_TRY(cudaGetDeviceProperties(&p, dev));
+        if (p.major != 10)
+            return fail(NOEL_ERR_NO_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                        p.major, p.minor);
+        c.sms = p.multiProcessorCount;
+        c.smem_optin = p.sharedMemPerBlockOptin;
+        void *k = nullptr, *v = nullptr, *o = nullptr;
+        CUDA_TRY(cudaGetSymbolAddress(&k, kExpfExcKeys));
+        CUDA_TRY(cudaGetSymbolAddress(&v, kExpfExcVals));
+        CUDA_TRY(cudaGetSymbolAddress(&o, kExpfExcOffs));
+        c.et.keys = static_cast<const uint32_t *>(k);
+        c.et.vals = static_cast<const uint32_t *>(v);
+        c.et.offs = static_cast<const uint32_t *>(o);
+        c.ready = true;
+    }
+    *out = &c;
+    return NOEL_OK;
+}
+
+/* Per-(device, stream) scratch of the exact kernel.  Calls on one stream run
+ * in order, so they can share it; calls on different streams get their own. */
+int workspace(DeviceCtx *c, cudaStream_t s, int rows, int vocab, Workspace **out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Workspace &w = c->ws[s];
+    const int nslots = rows < 64 ? rows : 64;
+    if (w.counters && rows <= w.rows_cap && vocab <= w.vocab_cap && nslots <= w.nslots) {
+        *out = &w;
+        return NOEL_OK;
+    }
+    if (w.counters) {
+        CUDA_TRY(cudaStreamSynchronize(s));
+        cudaFree(w.counters);
+        cudaFree(w.rows);
+        cudaFree(w.slots);
+        w = Workspace{};
+    }
+    const int rc = rows > 1 ? rows : 1, vc = vocab, ns = nslots > 1 ? nslots : 1;
+    CUDA_TRY(cudaMalloc(&w.counters, 4 * sizeof(int32_t)));
+    CUDA_TRY(cudaMemset(w.counters, 0, 4 * sizeof(int32_t)));
+    CUDA_TRY(cudaMalloc(&w.rows, (size_t)rc * sizeof(int32_t)));
+    CUDA_TRY(cudaMalloc(&w.slots, (size_t)ns * 2 * (size_t)vc * sizeof(uint2)));
+    w.rows_cap = rc;
+    w.vocab_cap = vc;
+    w.nslots = ns;
+    *out = &w;
+    return NOEL_OK;
+}
+
+int set_smem(DeviceCtx *c, const void *kernel, size_t bytes) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    size_t &cur = c->smem_set[kernel];
+    if (bytes > cur) {
+        CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+        cur = bytes;
+    }
+    return NOEL_OK;
+}
+
+int pow2_at_least(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+constexpr int kMaxKprime = 1024;  // top-k mode up to k = 1016
+constexpr int kCapMax = 4096;
+
+template <typename T>
+int launch_t(const SampleArgs &a0, int mode, size_t smem_main, size_t smem_exact, DeviceCtx *c,
+             cudaStream_t s) {
+    const void *kmain = nullptr;
+    if (mode == kGreedy) kmain = (const void *)sample_rows_kernel<T, kGreedy>;
+    else if (mode == kTopK) kmain = (const void *)sample_rows_kernel<T, kTopK>;
+    else kmain = (const void *)sample_rows_kernel<T, kFullList>;
+    const void *kexact = (const void *)exact_rows_kernel<T>;
+    int r = set_smem(c, kmain, smem_main);
+    if (r) return r;
+    r = set_smem(c, kexact, smem_exact);
+    if (r) return r;
+    if (mode == kGreedy) sample_rows_kernel<T, kGreedy><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
+    else if (mode == kTopK) sample_rows_kernel<T, kTopK><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
+    else sample_rows_kernel<T, kFullList><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
+    CUDA_TRY(cudaGetLastError());
+    if (mode != kGreedy) {
+        exact_rows_kernel<T><<<a0.nslots, kExactThreads, smem_exact, s>>>(a0);
+        CUDA_TRY(cudaGetLastError());
+    }
+    return NOEL_OK;
+}
+
+int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype, int B, int V,
+                 size_t ld, const int32_t *hist, int H, size_t hld, uint64_t *rng, int32_t *ids,
+                 const noel_sample_extras_t *ex, cudaStream_t s) {
+    if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
+    if (B < 0 || V <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", B, V);
+    if (B == 0) return ok();
+    if (!logits || !rng || !ids) return fail(NOEL_ERR_INVALID_ARG, "logits, rng and ids are required");
+    if (dtype != NOEL_DTYPE_F32 && dtype != NOEL_DTYPE_BF16) return fail(NOEL_ERR_INVALID_ARG, "dtype %d", dtype);
+    if (ld < (size_t)V) return fail(NOEL_ERR_INVALID_ARG, "ld %zu < vocab %d", ld, V);
+    const int es = dtype == NOEL_DTYPE_F32 ? 4 : 2;
+    if (reinterpret_cast<uintptr_t>(logits) % es) return fail(NOEL_ERR_INVALID_ARG, "logits not %d-byte aligned", es);
+    if (H < 0) return fail(NOEL_ERR_INVALID_ARG, "history_len %d", H);
+    if (hist && H > 0 && hld < (size_t)H) return fail(NOEL_ERR_INVALID_ARG, "hld %zu < history_len %d", hld, H);
+    if (ex && ex->list_len < 0) return fail(NOEL_ERR_INVALID_ARG, "list_len %d", ex->list_len);
+    if (ex && ex->write_back && dtype != NOEL_DTYPE_F32)
+        return fail(NOEL_ERR_UNSUPPORTED, "write_back needs fp32 logits");
+    if (ex && ex->d_stats && (reinterpret_cast<uintptr_t>(ex->d_stats) & 15))
+        return fail(NOEL_ERR_INVALID_ARG, "d_stats must be 16-byte aligned");
+
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+
+    SampleArgs a{};
+    a.logits = logits;
+    a.ld = (int64_t)ld;
+    a.vocab = V;
+    a.batch = B;
+    a.penalty = (cfg->repetition_penalty > 1.0f && hist && H > 0) ? 1 : 0;  // sampler.c:88
+    if (a.penalty) {
+        const int w = cfg->repetition_window;                                 // sampler.c:89-90
+        a.hist = hist;
+        a.hld = (int64_t)hld;
+        a.hist_len = H;
+        a.hist_start = (w > 0 && w < H) ? H - w : 0;
+    }
+    a.rep = cfg->repetition_penalty;
+    const float T = cfg->temperature;
+    a.inv_t = 1.0f / T;  // sampler.c:132
+    a.top_p = cfg->top_p;
+    a.top_k = cfg->top_k;
+    a.rng = rng;
+    a.ids = ids;
+    if (ex) {
+        a.probs = ex->d_probs;
+        a.list_ids = ex->d_list_ids;
+        a.list_probs = ex->d_list_probs;
+        a.list_len = ex->d_list_ids ? ex->list_len : 0;
+        a.list_weights = ex->list_weights;
+        a.stats = ex->d_stats;
+        if (ex->write_back && a.penalty) a.wb = const_cast<float *>(static_cast<const float *>(logits));
+    }
+    a.et = c->et;
+
+    int mode;
+    if (T <= 1e-4f) mode = kGreedy;  // sampler.c:106
+    else if (cfg->top_k > 0 && cfg->top_k <= kMaxKprime - 8) mode = kTopK;
+    else mode = kFullList;
+    if (mode == kTopK) {
+        a.kprime = pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
+        int cap = pow2_at_least(4 * a.kprime);
+        a.cap = cap < 512 ? 512 : (cap > kCapMax ? kCapMax : cap);
+    } else if (mode == kFullList) {
+        a.cap = kCapMax;
+    }
+
+    size_t hist_bytes = 0;
+    if (a.penalty) {
+        const size_t W = ((size_t)V + 31) / 32, G = (W + 7) / 8;
+        hist_bytes = W * 4 + (G + 1) * 4 + (size_t)(H - a.hist_start > 1 ? H - a.hist_start : 1) * 4;
+        hist_bytes = (hist_bytes + 15) & ~size_t(15);
+    }
+    size_t smem_main = hist_bytes;
+    if (mode != kGreedy) smem_main += (size_t)a.cap * 8;
+    if (mode == kTopK) smem_main += kWarmBins * 4;
+    const size_t smem_exact = a.penalty && !a.wb ? hist_bytes : 0;
+    if (smem_main > c->smem_optin - 2048 || smem_exact > c->smem_optin - 16384)
+        return fail(NOEL_ERR_TOO_LARGE, "vocab %d / history %d need %zu B of shared memory", V, H, smem_main);
+
+    if (mode != kGreedy) {
+        Workspace *w = nullptr;
+        r = workspace(c, s, B, V, &w);
+        if (r) return r;
+        a.counters = w->counters;
+        a.exact_list = w->rows;
+        a.slots = w->slots;
+        a.nslots = w->nslots;
+    }
+    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, smem_main, smem_exact, c, s)
+                                : launch_t<uint16_t>(a, mode, smem_main, smem_exact, c, s);
+    if (r) return r;
+    return ok();
+}
+
+/* ------------------------------------------- per-thread single-row state */
+struct Staging {
+    int dev = -1;
+    cudaStream_t stream = nullptr;
+    float *d_logits = nullptr;
+    size_t logits_cap = 0;
+    int32_t *d_hist = nullptr;
+    size_t hist_cap = 0;
+    uint64_t *d_rng = nullptr;
+    int32_t *d_out = nullptr;       // id, stats[4]
+    int32_t *d_list = nullptr;
+    float *d_listw = nullptr;
+    int list_cap = 0;
+    ~Staging() {
+        if (dev >= 0) {
+            cudaFree(d_logits);
+            cudaFree(d_hist);
+            cudaFree(d_rng);
+            cudaFree(d_out);
+            cudaFree(d_list);
+            cudaFree(d_listw);
+            if (stream) cudaStreamDestroy(stream);
+        }
+    }
+};
+thread_local Staging t_stage;
+
+int grow(void **p, size_t *cap, size_t need) {
+    if (*cap >= need) return NOEL_OK;
+    cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    CUDA_TRY(cudaMalloc(p, need));
+    *cap = need;
+    return NOEL_OK;
+}
+
+bool is_device_ptr(const void *p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+}  // namespace
+
+/* ========================================================================= */
+/* reference ABI (include/sampler.h)                                          */
+
+extern "C" void noel_sampler_init(noel_sampler_t *sampler, const noel_sampler_config_t *cfg, int max_vocab) {
+    if (!sampler) return;  // sampler.c:24
+    memset(sampler, 0, sizeof(*sampler));
+    if (cfg) {
+        sampler->config = *cfg;
+    } else {  // sampler.c:29-36
+        sampler->config.temperature = 0.7f;
+        sampler->config.top_p = 0.9f;
+        sampler->config.top_k = 40;
+        sampler->config.repetition_penalty = 1.1f;
+        sampler->config.repetition_window = 64;
+        sampler->config.seed = 0;
+    }
+    uint64_t seed = sampler->config.seed;  // sampler.c:38-47
+    if (seed == 0) seed = (uint64_t)time(NULL) ^ ((uint64_t)(uintptr_t)sampler << 16);
+    sampler->rng_state[0] = seed;
+    sampler->rng_state[1] = seed ^ 0x9E3779B97F4A7C15ULL;
+    if (sampler->rng_state[0] == 0 && sampler->rng_state[1] == 0) {
+        sampler->rng_state[0] = 123456789ULL;
+        sampler->rng_state[1] = 987654321ULL;
+    }
+    const int cap = max_vocab > 1024 ? max_vocab : 1024;  // sampler.c:49-51
+    sampler->candidates = (noel_token_prob_t *)malloc((size_t)cap * sizeof(noel_token_prob_t));
+    sampler->candidate_capacity = sampler->candidates ? cap : 0;
+}
+
+extern "C" void noel_sampler_free(noel_sampler_t *sampler) {
+    if (!sampler) return;  // sampler.c:54-61
+    free(sampler->candidates);
+    sampler->candidates = NULL;
+    sampler->candidate_capacity = 0;
+}
+
+extern "C" void noel_sampler_set_config(noel_sampler_t *sampler, const noel_sampler_config_t *cfg) {
+    if (!sampler || !cfg) return;  // sampler.c:63-70
+    sampler->config = *cfg;
+    if (cfg->seed != 0) {
+        sampler->rng_state[0] = cfg->seed;
+        sampler->rng_state[1] = cfg->seed ^ 0x9E3779B97F4A7C15ULL;
+    }
+}
+
+extern "C" float noel_sampler_random_f32(noel_sampler_t *sampler) {
+    if (!sampler) return 0.0f;  // sampler.c:17-21
+    uint64_t *s = sampler->rng_state;
+    uint64_t a = s[0];
+    const uint64_t b = s[1];
+    s[0] = b;
+    a ^= a << 23;
+    s[1] = a ^ b ^ (a >> 18) ^ (b >> 5);
+    return (float)((s[1] + b) >> 40) * (1.0f / 16777216.0f);
+}
+
+extern "C" int32_t noel_sampler_sample(noel_sampler_t *sampler, float *logits, int vocab_size,
+                                       const int32_t *history, int history_len) {
+    if (!sampler || !logits || vocab_size <= 0) {  // sampler.c:85
+        fail(NOEL_ERR_INVALID_ARG, "sampler, logits and vocab_size > 0 are required");
+        return 0;
+    }
+    Staging &st = t_stage;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        fail(NOEL_ERR_NO_DEVICE, "no CUDA device");
+        return 0;
+    }
+    if (st.dev != dev) {
+        st.~Staging();
+        new (&st) Staging();
+        st.dev = dev;
+        if (cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaMalloc(&st.d_rng, 2 * sizeof(uint64_t)) != cudaSuccess ||
+            cudaMalloc(&st.d_out, 8 * sizeof(int32_t)) != cudaSuccess) {
+            fail(NOEL_ERR_CUDA, "staging allocation failed");
+            st.dev = -1;
+            return 0;
+        }
+    }
+    cudaStream_t s = st.stream;
+    const bool dev_logits = is_device_ptr(logits);
+    const bool penalty = sampler->config.repetition_penalty > 1.0f && history && history_len > 0;
+    const size_t row_bytes = (size_t)vocab_size * sizeof(float);
+    float *d_row = logits;
+    if (!dev_logits) {
+        if (grow((void **)&st.d_logits, &st.logits_cap, row_bytes)) return 0;
+        d_row = st.d_logits;
+        if (cudaMemcpyAsync(d_row, logits, row_bytes, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+            fail(NOEL_ERR_CUDA, "row copy failed");
+            return 0;
+        }
+    }
+    const int32_t *d_hist = nullptr;
+    if (penalty) {
+        if (is_device_ptr(history)) {
+            d_hist = history;
+        } else {
+            if (grow((void **)&st.d_hist, &st.hist_cap, (size_t)history_len * sizeof(int32_t))) return 0;
+            if (cudaMemcpyAsync(st.d_hist, history, (size_t)history_len * sizeof(int32_t),
+                                cudaMemcpyHostToDevice, s) != cudaSuccess) {
+                fail(NOEL_ERR_CUDA, "history copy failed");
+                return 0;
+            }
+            d_hist = st.d_hist;
+        }
+    }
+    const int list = sampler->candidate_capacity < 4096 ? sampler->candidate_capacity : 4096;
+    if (list > st.list_cap) {
+        cudaFree(st.d_list);
+        cudaFree(st.d_listw);
+        st.d_list = nullptr;
+        st.d_listw = nullptr;
+        st.list_cap = 0;
+        if (cudaMalloc(&st.d_list, (size_t)list * 4) != cudaSuccess ||
+            cudaMalloc(&st.d_listw, (size_t)list * 4) != cudaSuccess) {
+            fail(NOEL_ERR_CUDA, "staging allocation failed");
+            return 0;
+        }
+        st.list_cap = list;
+    }
+    if (cudaMemcpyAsync(st.d_rng, sampler->rng_state, 16, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        fail(NOEL_ERR_CUDA, "state copy failed");
+        return 0;
+    }
+    noel_sample_extras_t ex{};
+    ex.d_list_ids = list > 0 ? st.d_list : nullptr;
+    ex.d_list_probs = list > 0 ? st.d_listw : nullptr;
+    ex.list_len = list;
+    ex.list_weights = 1;
+    ex.d_stats = st.d_out + 4;
+    ex.write_back = penalty ? 1 : 0;
+    if (sample_batch(&sampler->config, d_row, NOEL_DTYPE_F32, 1, vocab_size, (size_t)vocab_size, d_hist,
+                     penalty ? history_len : 0, (size_t)history_len, st.d_rng, st.d_out, &ex, s))
+        return 0;
+    int32_t out[8];
+    std::vector<int32_t> lid(list > 0 ? list : 0);
+    std::vector<float> lw(list > 0 ? list : 0);
+    cudaMemcpyAsync(out, st.d_out, sizeof(out), cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(sampler->rng_state, st.d_rng, 16, cudaMemcpyDeviceToHost, s);
+    if (list > 0) {
+        cudaMemcpyAsync(lid.data(), st.d_list, (size_t)list * 4, cudaMemcpyDeviceToHost, s);
+        cudaMemcpyAsync(lw.data(), st.d_listw, (size_t)list * 4, cudaMemcpyDeviceToHost, s);
+    }
+    if (penalty && !dev_logits) cudaMemcpyAsync(logits, d_row, row_bytes, cudaMemcpyDeviceToHost, s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        fail(NOEL_ERR_CUDA, "sampling failed: %s", cudaGetErrorString(e));
+        return 0;
+    }
+    const int nfinal = out[4 + NOEL_STAT_N_FINAL];
+    for (int i = 0; i < list && i < nfinal; ++i) {
+        sampler->candidates[i].id = lid[i];
+        sampler->candidates[i].val = lw[i];
+    }
+    ok();
+    return out[0];
+}
+
+/* ========================================================================= */
+/* batched entry points (include/noel_sampler_cuda.h)                         */
+
+extern "C" int noel_sampler_sample_batch(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
+                                         int batch, int vocab, size_t ld, const int32_t *d_history,
+                                         int history_len, size_t hld, uint64_t *d_rng, int32_t *d_ids,
+                                         float *d_probs, void *stream) {
+    noel_sample_extras_t ex{};
+    ex.d_probs = d_probs;
+    return sample_batch(cfg, d_logits, dtype, batch, vocab, ld, d_history, history_len, hld, d_rng, d_ids,
+                        &ex, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int noel_sampler_sample_batch_ex(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
+                                            int batch, int vocab, size_t ld, const int32_t *d_history,
+                                            int history_len, size_t hld, uint64_t *d_rng, int32_t *d_ids,
+                                            const noel_sample_extras_t *extras, void *stream) {
+    return sample_batch(cfg, d_logits, dtype, batch, vocab, ld, d_history, history_len, hld, d_rng, d_ids,
+                        extras, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+struct HostBatchStage {
+    int dev = -1;
+    cudaStream_t stream = nullptr;
+    void *d_logits = nullptr;
+    size_t logits_cap = 0;
+    void *d_hist = nullptr;
+    size_t hist_cap = 0;
+    void *d_rng = nullptr;
+    size_t rng_cap = 0;
+    void *d_ids = nullptr;
+    size_t ids_cap = 0;
+    void *d_probs = nullptr;
+    size_t probs_cap = 0;
+};
+thread_local HostBatchStage t_hb;
+}  // namespace
+
+extern "C" int noel_sampler_sample_batch_host(const noel_sampler_config_t *cfg, const void *h_logits, int dtype,
+                                              int batch, int vocab, size_t ld, const int32_t *h_history,
+                                              int history_len, size_t hld, uint64_t *h_rng, int32_t *h_ids,
+                                              float *h_probs) {
+    if (!cfg || !h_logits || !h_rng || !h_ids || batch < 0 || vocab <= 0 || ld < (size_t)vocab)
+        return fail(NOEL_ERR_INVALID_ARG, "invalid arguments");
+    if (dtype != NOEL_DTYPE_F32 && dtype != NOEL_DTYPE_BF16) return fail(NOEL_ERR_INVALID_ARG, "dtype %d", dtype);
+    if (batch == 0) return ok();
+    HostBatchStage &st = t_hb;
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    if (st.dev != dev) {
+        st = HostBatchStage{};
+        st.dev = dev;
+        CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
+    }
+    cudaStream_t s = st.stream;
+    const size_t es = dtype == NOEL_DTYPE_F32 ? 4 : 2;
+    const size_t row_bytes = (size_t)vocab * es;
+    int r;
+    if ((r = grow(&st.d_logits, &st.logits_cap, (size_t)batch * row_bytes))) return r;
+    if ((r = grow(&st.d_rng, &st.rng_cap, (size_t)batch * 16))) return r;
+    if ((r = grow(&st.d_ids, &st.ids_cap, (size_t)batch * 4))) return r;
+    if (h_probs && (r = grow(&st.d_probs, &st.probs_cap, (size_t)batch * 4))) return r;
+    if (ld == (size_t)vocab)
+        CUDA_TRY(cudaMemcpyAsync(st.d_logits, h_logits, (size_t)batch * row_bytes, cudaMemcpyHostToDevice, s));
+    else
+        CUDA_TRY(cudaMemcpy2DAsync(st.d_logits, row_bytes, h_logits, ld * es, row_bytes, batch,
+                                   cudaMemcpyHostToDevice, s));
+    const bool use_hist = h_history && history_len > 0;
+    if (use_hist) {
+        if ((r = grow(&st.d_hist, &st.hist_cap, (size_t)batch * history_len * 4))) return r;
+        CUDA_TRY(cudaMemcpy2DAsync(st.d_hist, (size_t)history_len * 4, h_history, hld * 4,
+                                   (size_t)history_len * 4, batch, cudaMemcpyHostToDevice, s));
+    }
+    CUDA_TRY(cudaMemcpyAsync(st.d_rng, h_rng, (size_t)batch * 16, cudaMemcpyHostToDevice, s));
+    noel_sample_extras_t ex{};
+    ex.d_probs = h_probs ? static_cast<float *>(st.d_probs) : nullptr;
+    r = sample_batch(cfg, st.d_logits, dtype, batch, vocab, (size_t)vocab,
+                     use_hist ? static_cast<const int32_t *>(st.d_hist) : nullptr, use_hist ? history_len : 0,
+                     (size_t)history_len, static_cast<uint64_t *>(st.d_rng), static_cast<int32_t *>(st.d_ids),
+                     &ex, s);
+    if (r) return r;
+    CUDA_TRY(cudaMemcpyAsync(h_ids, st.d_ids, (size_t)batch * 4, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaMemcpyAsync(h_rng, st.d_rng, (size_t)batch * 16, cudaMemcpyDeviceToHost, s));
+    if (h_probs) CUDA_TRY(cudaMemcpyAsync(h_probs, st.d_probs, (size_t)batch * 4, cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    return ok();
+}
+
+extern "C" int noel_sampler_cuda_last_error(void) { return t_status; }
+extern "C" const char *noel_sampler_cuda_last_error_message(void) { return t_msg; }
+extern "C" const char *noel_sampler_cuda_status_string(int status) {
+    switch (status) {
+        case NOEL_OK: return "ok";
+        case NOEL_ERR_INVALID_ARG: return "invalid argument";
+        case NOEL_ERR_CUDA: return "CUDA error";
+        case NOEL_ERR_NO_DEVICE: return "no usable device";
+        case NOEL_ERR_TOO_LARGE: return "size too large";
+        case NOEL_ERR_UNSUPPORTED: return "unsupported option";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int noel_sampler_cuda_expf_table_size(void) { return NOEL_EXPF_NEXC; }
+
+extern "C" int noel_sampler_cuda_expf_checksums(int chunk_log2, uint64_t *d_out, void *stream) {
+    if (!d_out || chunk_log2 < 10 || chunk_log2 > 30) return fail(NOEL_ERR_INVALID_ARG, "chunk_log2 %d", chunk_log2);
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    const uint64_t span = (uint64_t)(NOEL_EXPF_DOMAIN_END - NOEL_EXPF_DOMAIN_FIRST);
+    const unsigned nch = (unsigned)((span + (1ull << chunk_log2) - 1) >> chunk_log2);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    CUDA_TRY(cudaMemsetAsync(d_out, 0, (size_t)nch * 8, s));
+    dim3 grid(nch, 64);
+    expf_checksum_kernel<<<grid, 256, 0, s>>>(chunk_log2, d_out, c->et);
+    CUDA_TRY(cudaGetLastError());
+    return ok();
+}

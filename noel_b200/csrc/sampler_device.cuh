@@ -1,0 +1,546 @@
+/*
+ * Device code of the B200 token sampler (sm_100a).
+ *
+ * One pass of the reference sampler (Sain-Kai/noel src/sampler.c:80-192) per
+ * logits row, restructured for a GPU that streams rows from HBM:
+ *
+ *   sample_rows_kernel   one CTA per row.  Builds the row's history bitmap
+ *                        and per-id occurrence counts in shared memory,
+ *                        streams the row once with 128-bit loads, applies the
+ *                        penalty on the fly, and keeps a small candidate set
+ *                        in shared memory behind a rising threshold:
+ *                          greedy  - running argmax (sampler.c:106-116)
+ *                          top-k   - the K' = pow2(k+8) largest logits by
+ *                                    (logit desc, id asc), compacted by a
+ *                                    radix select whenever the buffer fills
+ *                          full    - every element that can still pass the
+ *                                    -15 cut under the running max
+ *                        then computes the reference's weights, sorts them
+ *                        by (weight desc, id asc), and runs the sequential
+ *                        mass / nucleus / draw loops of sampler.c:160-191.
+ *   exact_rows_kernel    rows the first kernel cannot finish exactly (a
+ *                        candidate set larger than shared memory, or a tie of
+ *                        weights at the top-k boundary reaching below the
+ *                        kept set) are redone here in two passes with the
+ *                        candidate list in global scratch and a stable radix
+ *                        sort, so every row's result is the reference's.
+ *
+ * Why selecting by logit is exact: the weight w = expf((x - max) * (1/T)) is
+ * non-decreasing in x (fp subtraction and multiplication by a positive are
+ * monotone; glibc's expf is monotone on (-15, 0], checked exhaustively), so
+ * the k-th largest weight is the weight of the k-th largest logit and every
+ * element outside the kept set has a weight <= the weight of the smallest
+ * kept logit.  When that weight is strictly below the k-th weight the kept
+ * set holds the whole top-k; otherwise the row is sent to the exact kernel.
+ */
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ref_expf.h"
+
+namespace noel {
+
+constexpr uint32_t kFull = 0xFFFFFFFFu;
+
+enum Mode { kGreedy = 0, kTopK = 1, kFullList = 2 };
+
+/* Flags kept per row in shared memory. */
+enum { kTruncated = 1, kOverflow = 2, kNeedExact = 4 };
+
+struct ExpTable {
+    const uint32_t *keys, *vals, *offs;
+};
+
+/* Kernel arguments (by value). */
+struct SampleArgs {
+    const void *logits;
+    int64_t ld;
+    int vocab, batch;
+    const int32_t *hist;
+    int64_t hld;
+    int hist_len, hist_start;   // window [hist_start, hist_len)
+    int penalty;                // repetition penalty active (sampler.c:88)
+    float rep;
+    float inv_t;                // 1.0f / temperature (sampler.c:132)
+    float top_p;
+    int top_k;
+    int kprime;                 // kept-set size for top-k
+    int cap;                    // candidate buffer entries
+    uint64_t *rng;
+    int32_t *ids;
+    float *probs;
+    int32_t *list_ids;
+    float *list_probs;
+    int list_len;
+    int list_weights;           // list_probs receives unnormalised weights
+    int32_t *stats;
+    float *wb;                  // penalised values written here (fp32 rows) or NULL
+    int32_t *exact_list;        // rows for exact_rows_kernel
+    int32_t *counters;          // [0] rows listed, [1] next row, [2] CTAs done
+    uint2 *slots;               // exact kernel scratch: nslots x 2 x vocab
+    int nslots;
+    ExpTable et;
+};
+
+/* ---------------------------------------------------------------------- */
+/* scalar helpers                                                          */
+
+/* order-preserving key of a non-NaN float; -0 and +0 share a key */
+__device__ __forceinline__ uint32_t ord_key(float x) {
+    const uint32_t u = __float_as_uint(__fadd_rn(x, 0.0f));
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+constexpr uint32_t kKeyNegInf = 0x007FFFFFu;   // ord_key(-inf)
+
+/* sampler.c:96-100 applied c times (one per occurrence in the window) */
+__device__ __forceinline__ float apply_penalty(float x, uint32_t c, float rep) {
+    for (uint32_t i = 0; i < c; ++i) x = (x > 0.0f) ? __fdiv_rn(x, rep) : __fmul_rn(x, rep);
+    return x;
+}
+
+/* sampler.c:8-21: xorshift128+ step, top 24 bits scaled by 2^-24 */
+__device__ __forceinline__ float rng_uniform(uint64_t *s) {
+    uint64_t a = s[0];
+    const uint64_t b = s[1];
+    s[0] = b;
+    a ^= a << 23;
+    s[1] = a ^ b ^ (a >> 18) ^ (b >> 5);
+    const uint64_t v = s[1] + b;
+    return __fmul_rn((float)(uint32_t)(v >> 40), 1.0f / 16777216.0f);
+}
+
+/* sampler.c:137: diff = (x - max) * inv_t, without contraction */
+__device__ __forceinline__ float scaled_diff(float x, float m, float inv_t) {
+    return __fmul_rn(__fsub_rn(x, m), inv_t);
+}
+
+__device__ __forceinline__ float ref_weight(float d, const ExpTable &et) {
+    return noel_ref_expf(d, et.keys, et.vals, et.offs);
+}
+
+/* ---------------------------------------------------------------------- */
+/* warp / block primitives                                                 */
+
+__device__ __forceinline__ int warp_incl_scan(int v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(kFull, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
+/* exclusive scan of one int per thread; s_w has NT/32+1 ints */
+template <int NT>
+__device__ __forceinline__ int block_excl_scan(int v, int *s_w, int &total) {
+    constexpr int NW = NT / 32;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int inc = warp_incl_scan(v);
+    if (lane == 31) s_w[w] = inc;
+    __syncthreads();
+    if (w == 0) {
+        const int x = lane < NW ? s_w[lane] : 0;
+        const int ix = warp_incl_scan(x);
+        if (lane < NW) s_w[lane] = ix - x;
+        if (lane == NW - 1) s_w[NW] = ix;
+    }
+    __syncthreads();
+    total = s_w[NW];
+    const int r = s_w[w] + inc - v;
+    __syncthreads();
+    return r;
+}
+
+template <int NT>
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v, uint32_t *s_w) {
+    constexpr int NW = NT / 32;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(kFull, v, o));
+    if ((threadIdx.x & 31) == 0) s_w[threadIdx.x >> 5] = v;
+    __syncthreads();
+    uint32_t r = s_w[0];
+    for (int i = 1; i < NW; ++i) r = max(r, s_w[i]);
+    __syncthreads();
+    return r;
+}
+
+template <int NT>
+__device__ __forceinline__ int block_sum_int(int v, int *s_w) {
+    int total;
+    block_excl_scan<NT>(v, s_w, total);
+    return total;
+}
+
+/* descending bitonic sort of P (power of two) 64-bit keys in shared memory */
+template <int NT>
+__device__ void bitonic_sort_desc(uint64_t *a, int P) {
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += NT) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t ai = a[i], aj = a[ixj];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (ai < aj) : (ai > aj)) {
+                        a[i] = aj;
+                        a[ixj] = ai;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+/* ---------------------------------------------------------------------- */
+/* history: bitmap of ids in the window, rank -> occurrence count           */
+
+struct HistView {
+    uint32_t *bm;    // ceil(V/32) words
+    uint32_t *gpre;  // set bits before each 8-word group; [G] = total
+    uint32_t *cnt;   // occurrences per distinct id, indexed by rank
+    int words;
+};
+
+__device__ __forceinline__ int hist_rank(const HistView &h, int t) {
+    const int w = t >> 5, g = t >> 8;
+    int r = (int)h.gpre[g];
+    for (int ww = g << 3; ww < w; ++ww) r += __popc(h.bm[ww]);
+    return r + __popc(h.bm[w] & ((1u << (t & 31)) - 1u));
+}
+
+/* sampler.c:88-93: the window of the row's history, ids in [0, V) only */
+template <int NT>
+__device__ void build_history(const HistView &h, const int32_t *hrow, int first, int H, int V,
+                              int *s_w) {
+    const int W = h.words, G = (W + 7) >> 3;
+    for (int i = threadIdx.x; i < W; i += NT) h.bm[i] = 0u;
+    __syncthreads();
+    for (int i = first + threadIdx.x; i < H; i += NT) {
+        const int t = hrow[i];
+        if (t >= 0 && t < V) atomicOr(&h.bm[t >> 5], 1u << (t & 31));
+    }
+    __syncthreads();
+    const int per = (G + NT - 1) / NT;
+    const int g0 = threadIdx.x * per, g1 = min(G, g0 + per);
+    int mine = 0;
+    for (int g = g0; g < g1; ++g) {
+        int s = 0;
+        for (int w = g * 8; w < min(W, g * 8 + 8); ++w) s += __popc(h.bm[w]);
+        h.gpre[g] = (uint32_t)s;
+        mine += s;
+    }
+    int total;
+    int base = block_excl_scan<NT>(mine, s_w, total);
+    for (int g = g0; g < g1; ++g) {
+        const int s = (int)h.gpre[g];
+        h.gpre[g] = (uint32_t)base;
+        base += s;
+    }
+    if (threadIdx.x == 0) h.gpre[G] = (uint32_t)total;
+    for (int i = threadIdx.x; i < total; i += NT) h.cnt[i] = 0u;
+    __syncthreads();
+    for (int i = first + threadIdx.x; i < H; i += NT) {
+        const int t = hrow[i];
+        if (t >= 0 && t < V) atomicAdd(&h.cnt[hist_rank(h, t)], 1u);
+    }
+    __syncthreads();
+}
+
+/* penalty bits of ids [id0, id0+n) (n <= 16) */
+__device__ __forceinline__ uint32_t hist_bits(const HistView &h, int id0, int n) {
+    const int w = id0 >> 5, sh = id0 & 31;
+    uint32_t b = h.bm[w] >> sh;
+    if (sh + n > 32 && w + 1 < h.words) b |= h.bm[w + 1] << (32 - sh);
+    return b & ((1u << n) - 1u);
+}
+
+/* ---------------------------------------------------------------------- */
+/* element formats                                                          */
+
+/* 32-byte vector: Blackwell loads 256 bits per thread in one instruction */
+struct alignas(32) V8 {
+    uint32_t v[8];
+};
+
+template <typename T>
+struct Fmt;
+template <>
+struct Fmt<float> {
+    static constexpr int VEC = 8, ES = 4, U = 4;
+    __device__ static __forceinline__ void unpack(const V8 &v, float *x) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = __uint_as_float(v.v[i]);
+    }
+    __device__ static __forceinline__ float scalar(const void *row, int i) {
+        return static_cast<const float *>(row)[i];
+    }
+};
+template <>
+struct Fmt<uint16_t> {  // bf16 bit patterns; upcast is exact
+    static constexpr int VEC = 16, ES = 2, U = 2;
+    __device__ static __forceinline__ void unpack(const V8 &v, float *x) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            x[2 * i] = __uint_as_float(v.v[i] << 16);
+            x[2 * i + 1] = __uint_as_float(v.v[i] & 0xFFFF0000u);
+        }
+    }
+    __device__ static __forceinline__ float scalar(const void *row, int i) {
+        return __uint_as_float((uint32_t)static_cast<const uint16_t *>(row)[i] << 16);
+    }
+};
+
+/* streaming 256-bit load that keeps the row out of L1 and evicts it first from L2 */
+__device__ __forceinline__ V8 ld_stream(const V8 *p) {
+    V8 r;
+    asm volatile(
+        "ld.global.nc.L1::no_allocate.L2::evict_first.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]),
+          "=r"(r.v[6]), "=r"(r.v[7])
+        : "l"(p));
+    return r;
+}
+
+/* Row geometry: scalar head until 32-byte alignment, vector body, scalar tail. */
+struct RowGeom {
+    int head, nvec, tail0, nscalar;
+};
+template <typename T>
+__device__ __forceinline__ RowGeom row_geom(const void *row, int V) {
+    using F = Fmt<T>;
+    RowGeom g;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(row);
+    g.head = (int)(((32u - (a & 31u)) & 31u) / F::ES);
+    if (g.head > V) g.head = V;
+    g.nvec = (V - g.head) / F::VEC;
+    g.tail0 = g.head + g.nvec * F::VEC;
+    g.nscalar = g.head + (V - g.tail0);
+    return g;
+}
+__device__ __forceinline__ int scalar_id(const RowGeom &g, int s) {
+    return s < g.head ? s : g.tail0 + (s - g.head);
+}
+
+/* ---------------------------------------------------------------------- */
+/* candidate buffer and its compaction                                      */
+
+struct Buf {
+    uint32_t *key;  // ord_key of the (penalised) logit
+    uint32_t *id;
+};
+
+struct SelShared {
+    uint32_t hist[256];
+    int digit, above, eq;
+};
+
+/*
+ * Keep the K largest entries by (key desc, id asc); entries land in [0, K).
+ * Returns the K-th key; *id_thr is the largest kept id among entries with
+ * that key when ties had to be cut, else 0xFFFFFFFF.
+ */
+template <int NT, int EPT>
+__device__ uint32_t select_top(Buf b, int n, int K, SelShared &ss, int *s_w, uint32_t *id_thr) {
+    uint32_t prefix = 0, mask = 0;
+    int need = K;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += NT) ss.hist[i] = 0u;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += NT) {
+            const uint32_t k = b.key[i];
+            if ((k & mask) == prefix) atomicAdd(&ss.hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            int c[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {  // lane covers digits 255-8*lane .. 248-8*lane
+                c[j] = (int)ss.hist[255 - 8 * lane - j];
+                s += c[j];
+            }
+            const int inc = warp_incl_scan(s);
+            const int before = inc - s;
+            if (before < need && need <= inc) {
+                int cum = before;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (cum < need && need <= cum + c[j]) {
+                        ss.digit = 255 - 8 * lane - j;
+                        ss.above = cum;
+                        ss.eq = c[j];
+                    }
+                    cum += c[j];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= (uint32_t)ss.digit << shift;
+        mask |= 0xFFu << shift;
+        need -= ss.above;
+        __syncthreads();
+    }
+    const uint32_t t = prefix;
+    const int eq = ss.eq;
+    uint32_t ithr = 0xFFFFFFFFu;
+    if (eq > need) {  // cut ties at t by ascending id
+        uint32_t ip = 0, im = 0;
+        int need2 = need;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int i = threadIdx.x; i < 256; i += NT) ss.hist[i] = 0u;
+            __syncthreads();
+            for (int i = threadIdx.x; i < n; i += NT) {
+                const uint32_t id = b.id[i];
+                if (b.key[i] == t && (id & im) == ip) atomicAdd(&ss.hist[(id >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (threadIdx.x < 32) {
+                const int lane = threadIdx.x;
+                int c[8], s = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    c[j] = (int)ss.hist[8 * lane + j];
+                    s += c[j];
+                }
+                const int inc = warp_incl_scan(s);
+                const int before = inc - s;
+                if (before < need2 && need2 <= inc) {
+                    int cum = before;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (cum < need2 && need2 <= cum + c[j]) {
+                            ss.digit = 8 * lane + j;
+                            ss.above = cum;
+                        }
+                        cum += c[j];
+                    }
+                }
+            }
+            __syncthreads();
+            ip |= (uint32_t)ss.digit << shift;
+            im |= 0xFFu << shift;
+            need2 -= ss.above;
+            __syncthreads();
+        }
+        ithr = ip;
+    }
+    /* stable in-place compaction of the kept entries */
+    uint32_t kk[EPT], ki[EPT];
+    const int per = (n + NT - 1) / NT;
+    const int i0 = threadIdx.x * per;
+    int mine = 0;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+        const int i = i0 + e;
+        kk[e] = 0u;
+        ki[e] = 0u;
+        if (e < per && i < n) {
+            kk[e] = b.key[i];
+            ki[e] = b.id[i];
+            if (kk[e] > t || (kk[e] == t && ki[e] <= ithr)) ++mine;
+        }
+    }
+    int total;
+    int pos = block_excl_scan<NT>(mine, s_w, total);  // its barriers order reads before writes
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+        const int i = i0 + e;
+        if (e < per && i < n && (kk[e] > t || (kk[e] == t && ki[e] <= ithr))) {
+            b.key[pos] = kk[e];
+            b.id[pos] = ki[e];
+            ++pos;
+        }
+    }
+    __syncthreads();
+    *id_thr = ithr;
+    return t;
+}
+
+/* Full-list mode: drop entries that fail the -15 cut under max m. */
+template <int NT, int EPT>
+__device__ int filter_by_max(Buf b, int n, float m, float inv_t, int *s_w) {
+    uint32_t kk[EPT], ki[EPT];
+    const int per = (n + NT - 1) / NT;
+    const int i0 = threadIdx.x * per;
+    int mine = 0;
+    bool keep[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+        const int i = i0 + e;
+        keep[e] = false;
+        kk[e] = 0u;
+        ki[e] = 0u;
+        if (e < per && i < n) {
+            kk[e] = b.key[i];
+            ki[e] = b.id[i];
+            keep[e] = scaled_diff(key_float(kk[e]), m, inv_t) > -15.0f;
+            mine += keep[e];
+        }
+    }
+    int total;
+    int pos = block_excl_scan<NT>(mine, s_w, total);
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+        if (keep[e]) {
+            b.key[pos] = kk[e];
+            b.id[pos] = ki[e];
+            ++pos;
+        }
+    }
+    __syncthreads();
+    return total;
+}
+
+/* ---------------------------------------------------------------------- */
+/* the sequential tail of sampler.c:155-191 over a sorted weight list       */
+
+struct TailOut {
+    int n_topk, n_final, pos;
+    float mass;
+};
+
+/* w(i) returns the i-th weight of the list sorted by (weight desc, id asc) */
+template <typename WeightAt>
+__device__ __forceinline__ TailOut run_tail(int num_cands, bool more_than_listed, int top_k,
+                                            float top_p, uint64_t *rng, WeightAt w) {
+    TailOut o;
+    int n = num_cands;
+    if (top_k > 0 && (more_than_listed || top_k < n)) n = top_k;  // sampler.c:155-157
+    o.n_topk = n;
+    float mass = 0.0f;                                             // sampler.c:160-163
+    for (int i = 0; i < n; ++i) mass = __fadd_rn(mass, w(i));
+    if (top_p > 0.0f && top_p < 1.0f) {                            // sampler.c:165-179
+        const float cutoff = __fmul_rn(top_p, mass);
+        float cum = 0.0f;
+        int keep = 0;
+        for (int i = 0; i < n; ++i) {
+            cum = __fadd_rn(cum, w(i));
+            ++keep;
+            if (cum >= cutoff) break;
+        }
+        n = keep;
+        mass = cum;
+    }
+    o.n_final = n;
+    o.mass = mass;
+    const float r = __fmul_rn(rng_uniform(rng), mass);            // sampler.c:182-191
+    float acc = 0.0f;
+    o.pos = n - 1;
+    for (int i = 0; i < n; ++i) {
+        acc = __fadd_rn(acc, w(i));
+        if (r <= acc) {
+            o.pos = i;
+            break;
+        }
+    }
+    return o;
+}
+
+}  // namespace noel

@@ -1,0 +1,277 @@
+"""Python front end of libnoel_sampler_cuda.so (ctypes over the C ABI).
+
+Mirrors the reference sampler's interface (Sain-Kai/noel include/sampler.h):
+``Sampler`` wraps ``noel_sampler_t`` with the same init / set_config / sample
+/ random_f32 / free semantics, and ``sample_batch`` exposes the batched
+device entry point for torch tensors already on the GPU.  There is no CPU
+path: loading fails loudly if the library has not been built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from .build import LIB
+
+F32, BF16 = 0, 1
+
+STAT_NUM_CANDS, STAT_N_TOPK, STAT_N_FINAL, STAT_FLAGS = range(4)
+ROW_GREEDY, ROW_EXACT_PASS, ROW_FALLBACK = 1, 2, 4
+
+
+class SamplerConfig(C.Structure):
+    """noel_sampler_config_t (include/sampler.h; reference include/sampler.h:12-19)."""
+
+    _fields_ = [
+        ("temperature", C.c_float),
+        ("top_p", C.c_float),
+        ("top_k", C.c_int),
+        ("repetition_penalty", C.c_float),
+        ("repetition_window", C.c_int),
+        ("seed", C.c_uint64),
+    ]
+
+
+class TokenProb(C.Structure):
+    _fields_ = [("id", C.c_int32), ("val", C.c_float)]
+
+
+class SamplerStruct(C.Structure):
+    """noel_sampler_t (reference include/sampler.h:26-31)."""
+
+    _fields_ = [
+        ("config", SamplerConfig),
+        ("rng_state", C.c_uint64 * 2),
+        ("candidates", C.POINTER(TokenProb)),
+        ("candidate_capacity", C.c_int),
+    ]
+
+
+class Extras(C.Structure):
+    _fields_ = [
+        ("d_probs", C.c_void_p),
+        ("d_list_ids", C.c_void_p),
+        ("d_list_probs", C.c_void_p),
+        ("list_len", C.c_int),
+        ("list_weights", C.c_int),
+        ("d_stats", C.c_void_p),
+        ("write_back", C.c_int),
+    ]
+
+
+class NoelSamplerError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"noel sampler status {status}: {message}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load the in-tree library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB):
+        raise FileNotFoundError(f"{LIB} is missing: run `python -m noel_b200.build`")
+    L = C.CDLL(LIB)
+    L.noel_sampler_init.restype = None
+    L.noel_sampler_init.argtypes = [C.POINTER(SamplerStruct), C.POINTER(SamplerConfig), C.c_int]
+    L.noel_sampler_free.restype = None
+    L.noel_sampler_free.argtypes = [C.POINTER(SamplerStruct)]
+    L.noel_sampler_set_config.restype = None
+    L.noel_sampler_set_config.argtypes = [C.POINTER(SamplerStruct), C.POINTER(SamplerConfig)]
+    L.noel_sampler_sample.restype = C.c_int32
+    L.noel_sampler_sample.argtypes = [C.POINTER(SamplerStruct), C.c_void_p, C.c_int, C.c_void_p, C.c_int]
+    L.noel_sampler_random_f32.restype = C.c_float
+    L.noel_sampler_random_f32.argtypes = [C.POINTER(SamplerStruct)]
+    L.noel_sampler_sample_batch.restype = C.c_int
+    L.noel_sampler_sample_batch.argtypes = [
+        C.POINTER(SamplerConfig), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p,
+        C.c_int, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+    ]
+    L.noel_sampler_sample_batch_ex.restype = C.c_int
+    L.noel_sampler_sample_batch_ex.argtypes = [
+        C.POINTER(SamplerConfig), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p,
+        C.c_int, C.c_size_t, C.c_void_p, C.c_void_p, C.POINTER(Extras), C.c_void_p,
+    ]
+    L.noel_sampler_sample_batch_host.restype = C.c_int
+    L.noel_sampler_sample_batch_host.argtypes = [
+        C.POINTER(SamplerConfig), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p,
+        C.c_int, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p,
+    ]
+    L.noel_sampler_cuda_last_error.restype = C.c_int
+    L.noel_sampler_cuda_last_error_message.restype = C.c_char_p
+    L.noel_sampler_cuda_status_string.restype = C.c_char_p
+    L.noel_sampler_cuda_status_string.argtypes = [C.c_int]
+    L.noel_sampler_cuda_expf_table_size.restype = C.c_int
+    L.noel_sampler_cuda_expf_checksums.restype = C.c_int
+    L.noel_sampler_cuda_expf_checksums.argtypes = [C.c_int, C.c_void_p, C.c_void_p]
+    _lib = L
+    return L
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = lib().noel_sampler_cuda_last_error_message().decode(errors="replace")
+        raise NoelSamplerError(status, msg)
+
+
+def make_config(temperature=0.7, top_p=0.9, top_k=40, repetition_penalty=1.1,
+                repetition_window=64, seed=0) -> SamplerConfig:
+    return SamplerConfig(float(temperature), float(top_p), int(top_k), float(repetition_penalty),
+                         int(repetition_window), int(seed))
+
+
+class Sampler:
+    """One noel_sampler_t, driven through the reference ABI."""
+
+    def __init__(self, cfg: SamplerConfig | None = None, max_vocab: int = 1024):
+        self.s = SamplerStruct()
+        lib().noel_sampler_init(C.byref(self.s), C.byref(cfg) if cfg is not None else None, max_vocab)
+
+    @property
+    def config(self) -> SamplerConfig:
+        return self.s.config
+
+    @property
+    def rng_state(self) -> tuple[int, int]:
+        return (self.s.rng_state[0], self.s.rng_state[1])
+
+    @rng_state.setter
+    def rng_state(self, st) -> None:
+        self.s.rng_state[0], self.s.rng_state[1] = int(st[0]), int(st[1])
+
+    def set_config(self, cfg: SamplerConfig) -> None:
+        lib().noel_sampler_set_config(C.byref(self.s), C.byref(cfg))
+
+    def random_f32(self) -> float:
+        return lib().noel_sampler_random_f32(C.byref(self.s))
+
+    def sample(self, logits, history=None) -> int:
+        """logits: float32 numpy array (host, modified in place when the
+        penalty applies) or a CUDA torch tensor; history: int32 array/tensor."""
+        lp, V = _ptr_len(logits)
+        hp, H = _ptr_len(history) if history is not None else (None, 0)
+        r = lib().noel_sampler_sample(C.byref(self.s), lp, V, hp, H)
+        st = lib().noel_sampler_cuda_last_error()
+        if st != 0:
+            _check(st)
+        return int(r)
+
+    def candidates(self, n: int) -> list[tuple[int, float]]:
+        return [(self.s.candidates[i].id, self.s.candidates[i].val) for i in range(n)]
+
+    def free(self) -> None:
+        lib().noel_sampler_free(C.byref(self.s))
+
+    def __del__(self):
+        try:
+            if self.s.candidates:
+                self.free()
+        except Exception:
+            pass
+
+
+def _ptr_len(a):
+    if a is None:
+        return None, 0
+    if isinstance(a, np.ndarray):
+        assert a.flags.c_contiguous
+        return a.ctypes.data, a.size
+    return a.data_ptr(), a.numel()  # torch tensor
+
+
+def sample_batch(logits, rng, cfg: SamplerConfig, history=None, probs: bool = True,
+                 list_len: int = 0, list_weights: bool = False, stats: bool = False,
+                 write_back: bool = False, vocab: int | None = None, stream=None):
+    """Batched device sampling of torch tensors on the current CUDA device.
+
+    logits: [B, ld] float32 or bfloat16 (row stride ld >= vocab, unit column
+    stride); rng: [B, 2] int64 xorshift128+ states, advanced in place;
+    history: [B, hld] int32 or None.  Returns a dict of torch tensors:
+    ids [B] int32, and as requested probs [B], list_ids/list_probs
+    [B, list_len], stats [B, 4].
+    """
+    import torch
+
+    assert logits.is_cuda and logits.dim() == 2 and logits.stride(1) == 1
+    B, ld = logits.shape[0], logits.stride(0)
+    V = logits.shape[1] if vocab is None else vocab
+    dtype = {torch.float32: F32, torch.bfloat16: BF16}[logits.dtype]
+    assert rng.dtype == torch.int64 and rng.shape == (B, 2) and rng.is_contiguous()
+    dev = logits.device
+    out = {"ids": torch.empty(B, dtype=torch.int32, device=dev)}
+    ex = Extras()
+    if probs:
+        out["probs"] = torch.empty(B, dtype=torch.float32, device=dev)
+        ex.d_probs = out["probs"].data_ptr()
+    if list_len:
+        out["list_ids"] = torch.empty(B, list_len, dtype=torch.int32, device=dev)
+        out["list_probs"] = torch.empty(B, list_len, dtype=torch.float32, device=dev)
+        ex.d_list_ids = out["list_ids"].data_ptr()
+        ex.d_list_probs = out["list_probs"].data_ptr()
+        ex.list_len = list_len
+        ex.list_weights = 1 if list_weights else 0
+    if stats:
+        out["stats"] = torch.empty(B, 4, dtype=torch.int32, device=dev)
+        ex.d_stats = out["stats"].data_ptr()
+    ex.write_back = 1 if write_back else 0
+    if history is not None:
+        assert history.is_cuda and history.dtype == torch.int32 and history.stride(1) == 1
+        hp, H, hld = history.data_ptr(), history.shape[1], history.stride(0)
+    else:
+        hp, H, hld = None, 0, 0
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    _check(lib().noel_sampler_sample_batch_ex(C.byref(cfg), logits.data_ptr(), dtype, B, V, ld, hp, H, hld,
+                                              rng.data_ptr(), out["ids"].data_ptr(), C.byref(ex),
+                                              C.c_void_p(s.cuda_stream)))
+    return out
+
+
+def sample_batch_raw(cfg: SamplerConfig, logits_ptr: int, dtype: int, B: int, V: int, ld: int,
+                     hist_ptr, H: int, hld: int, rng_ptr: int, ids_ptr: int, probs_ptr, stream_ptr) -> None:
+    """Thin pass-through to noel_sampler_sample_batch (pointers as ints)."""
+    _check(lib().noel_sampler_sample_batch(C.byref(cfg), logits_ptr, dtype, B, V, ld, hist_ptr, H, hld,
+                                           rng_ptr, ids_ptr, probs_ptr, C.c_void_p(stream_ptr)))
+
+
+def sample_batch_host(cfg: SamplerConfig, logits: np.ndarray, rng: np.ndarray, history: np.ndarray | None = None,
+                      probs: bool = False, vocab: int | None = None):
+    """Host-buffer batched sampling (noel_sampler_sample_batch_host).
+    logits: [B, ld] float32, or uint16 holding bf16 bits; rng [B, 2] uint64
+    (advanced in place).  Returns ids (and probs)."""
+    B, ld = logits.shape
+    V = ld if vocab is None else vocab
+    dtype = BF16 if logits.dtype == np.uint16 else F32
+    assert logits.flags.c_contiguous and rng.flags.c_contiguous and rng.dtype == np.uint64
+    ids = np.empty(B, np.int32)
+    pr = np.empty(B, np.float32) if probs else None
+    if history is not None:
+        assert history.dtype == np.int32 and history.flags.c_contiguous
+        hp, H, hld = history.ctypes.data, history.shape[1], history.shape[1]
+    else:
+        hp, H, hld = None, 0, 0
+    _check(lib().noel_sampler_sample_batch_host(C.byref(cfg), logits.ctypes.data, dtype, B, V, ld, hp, H, hld,
+                                                rng.ctypes.data, ids.ctypes.data,
+                                                pr.ctypes.data if pr is not None else None))
+    return (ids, pr) if probs else ids
+
+
+def expf_table_size() -> int:
+    return lib().noel_sampler_cuda_expf_table_size()
+
+
+def expf_checksums(chunk_log2: int = 24):
+    """Device exp-weight checksums over (-15, 0] (see include/noel_sampler_cuda.h)."""
+    import torch
+
+    n = -(-(0xC1700000 - 0x80000000) // (1 << chunk_log2))
+    out = torch.empty(n, dtype=torch.int64, device="cuda")
+    s = torch.cuda.current_stream()
+    _check(lib().noel_sampler_cuda_expf_checksums(chunk_log2, out.data_ptr(), C.c_void_p(s.cuda_stream)))
+    s.synchronize()
+    return out.cpu().numpy().view(np.uint64)

@@ -1,0 +1,239 @@
+"""ctypes front end of the CPU checkers (test infrastructure only).
+
+* ``Oracle`` wraps ``oracle/liboracle.so``: the restatement of the reference
+  sampler (Sain-Kai/noel src/sampler.c:8-192) in ``sampler_oracle.c``.
+* ``RefSampler`` wraps ``oracle/_ref/libsampler_ref.so``: the reference
+  sampler itself, compiled from its own sources by ``oracle/Makefile``.
+
+Only tests/, ``__graft_entry__.smoke()`` and the cpu_baseline leg of
+bench.py import this module; the library under ``noel_b200`` never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libsampler_ref.so")
+
+
+class SamplerConfig(C.Structure):
+    """Byte-compatible with noel_sampler_config_t (include/sampler.h:12-19)."""
+
+    _fields_ = [
+        ("temperature", C.c_float),
+        ("top_p", C.c_float),
+        ("top_k", C.c_int),
+        ("repetition_penalty", C.c_float),
+        ("repetition_window", C.c_int),
+        ("seed", C.c_uint64),
+    ]
+
+
+DIAG_DTYPE = np.dtype(
+    [
+        ("id", np.int32),
+        ("greedy", np.int32),
+        ("num_cands", np.int32),
+        ("n_topk", np.int32),
+        ("n_final", np.int32),
+        ("pos", np.int32),
+        ("max_val", np.float32),
+        ("total_mass", np.float32),
+        ("u", np.float32),
+        ("r", np.float32),
+    ]
+)
+
+
+def make_config(temperature=0.7, top_p=0.9, top_k=40, repetition_penalty=1.1,
+                repetition_window=64, seed=0) -> SamplerConfig:
+    return SamplerConfig(float(temperature), float(top_p), int(top_k),
+                         float(repetition_penalty), int(repetition_window), int(seed))
+
+
+def build(quiet: bool = True) -> None:
+    """Compile the checkers (``make -C oracle``)."""
+    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
+    if not quiet:
+        print(out.stdout)
+
+
+def _ptr(a, ctype):
+    return None if a is None else a.ctypes.data_as(C.POINTER(ctype))
+
+
+def seed_states(seeds) -> np.ndarray:
+    """Per-row xorshift128+ states for non-zero seeds (sampler.c:42-47)."""
+    seeds = np.asarray(seeds, dtype=np.uint64)
+    st = np.empty((seeds.size, 2), dtype=np.uint64)
+    st[:, 0] = seeds
+    st[:, 1] = seeds ^ np.uint64(0x9E3779B97F4A7C15)
+    zero = (st[:, 0] == 0) & (st[:, 1] == 0)
+    st[zero, 0] = 123456789
+    st[zero, 1] = 987654321
+    return st
+
+
+@dataclass
+class BatchResult:
+    ids: np.ndarray
+    rng: np.ndarray
+    probs: np.ndarray | None = None
+    diag: np.ndarray | None = None
+    topn_ids: np.ndarray | None = None
+    topn_probs: np.ndarray | None = None
+    num_cands: np.ndarray | None = None
+    cand_vals: np.ndarray | None = None
+
+
+class Oracle:
+    """The restatement (sampler_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build()
+        self.lib = C.CDLL(path)
+        L = self.lib
+        L.orc_sample_batch.restype = None
+        L.orc_sample_batch.argtypes = [
+            C.POINTER(SamplerConfig), C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t,
+            C.POINTER(C.c_int32), C.c_int, C.c_size_t, C.POINTER(C.c_uint64),
+            C.POINTER(C.c_int32), C.POINTER(C.c_float), C.c_void_p,
+            C.POINTER(C.c_int32), C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int,
+        ]
+        L.orc_sample_batch_bf16.restype = None
+        L.orc_sample_batch_bf16.argtypes = [
+            C.POINTER(SamplerConfig), C.POINTER(C.c_uint16), C.c_int, C.c_int, C.c_size_t,
+            C.POINTER(C.c_int32), C.c_int, C.c_size_t, C.POINTER(C.c_uint64),
+            C.POINTER(C.c_int32), C.POINTER(C.c_float), C.c_void_p,
+            C.POINTER(C.c_int32), C.POINTER(C.c_float), C.c_int, C.c_int,
+        ]
+        L.orc_random_f32.restype = C.c_float
+        L.orc_random_f32.argtypes = [C.POINTER(C.c_uint64)]
+        L.orc_expf_range.restype = None
+        L.orc_expf_range.argtypes = [C.c_uint32, C.c_uint32, C.POINTER(C.c_float)]
+        L.orc_expf_domain_checksums.restype = None
+        L.orc_expf_domain_checksums.argtypes = [C.c_int, C.POINTER(C.c_uint64), C.c_int, C.c_int]
+
+    def sample_batch(self, cfg: SamplerConfig, logits: np.ndarray, vocab: int | None = None,
+                     history: np.ndarray | None = None, rng: np.ndarray | None = None,
+                     n_list: int = 0, nthreads: int = 0, in_place: bool = False) -> BatchResult:
+        """logits: [B, ld] float32, or uint16 holding bf16 bits."""
+        B, ld = logits.shape
+        V = ld if vocab is None else vocab
+        rng = np.ascontiguousarray(rng.copy() if rng is not None else seed_states(np.arange(1, B + 1)),
+                                   dtype=np.uint64)
+        assert rng.shape == (B, 2)
+        ids = np.empty(B, np.int32)
+        probs = np.empty(B, np.float32)
+        diag = np.empty(B, DIAG_DTYPE)
+        tn_ids = np.empty((B, max(n_list, 1)), np.int32) if n_list else None
+        tn_p = np.empty((B, max(n_list, 1)), np.float32) if n_list else None
+        if history is not None:
+            history = np.ascontiguousarray(history, dtype=np.int32)
+            H, hld = history.shape[1], history.shape[1]
+        else:
+            H, hld = 0, 0
+        if logits.dtype == np.uint16:
+            lg = np.ascontiguousarray(logits)
+            self.lib.orc_sample_batch_bf16(C.byref(cfg), _ptr(lg, C.c_uint16), B, V, ld,
+                                           _ptr(history, C.c_int32), H, hld, _ptr(rng, C.c_uint64),
+                                           _ptr(ids, C.c_int32), _ptr(probs, C.c_float),
+                                           diag.ctypes.data, _ptr(tn_ids, C.c_int32),
+                                           _ptr(tn_p, C.c_float), n_list, nthreads)
+        else:
+            lg = logits if in_place else np.ascontiguousarray(logits, dtype=np.float32)
+            assert lg.dtype == np.float32 and lg.flags.c_contiguous
+            self.lib.orc_sample_batch(C.byref(cfg), _ptr(lg, C.c_float), B, V, ld,
+                                      _ptr(history, C.c_int32), H, hld, _ptr(rng, C.c_uint64),
+                                      _ptr(ids, C.c_int32), _ptr(probs, C.c_float), diag.ctypes.data,
+                                      _ptr(tn_ids, C.c_int32), _ptr(tn_p, C.c_float), n_list,
+                                      1 if in_place else 0, nthreads)
+        return BatchResult(ids=ids, rng=rng, probs=probs, diag=diag, topn_ids=tn_ids, topn_probs=tn_p)
+
+    def expf(self, x: np.ndarray) -> np.ndarray:
+        """glibc expf on an arbitrary float32 array (via contiguous bit ranges)."""
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        out = np.empty_like(x)
+        buf = np.empty(1, np.float32)
+        for i, b in enumerate(x.view(np.uint32)):
+            self.lib.orc_expf_range(int(b), 1, _ptr(buf, C.c_float))
+            out[i] = buf[0]
+        return out
+
+    def expf_range(self, lo_bits: int, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.lib.orc_expf_range(lo_bits, n, _ptr(out, C.c_float))
+        return out
+
+    def expf_domain_checksums(self, chunk_log2: int = 24, nthreads: int = 0) -> np.ndarray:
+        n = -(-(0xC1700000 - 0x80000000) // (1 << chunk_log2))
+        out = np.empty(n, np.uint64)
+        self.lib.orc_expf_domain_checksums(chunk_log2, _ptr(out, C.c_uint64), n, nthreads)
+        return out
+
+
+class RefSampler:
+    """The reference sampler itself (oracle/_ref/libsampler_ref.so)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = C.CDLL(path)
+        L = self.lib
+        L.ref_sample_batch.restype = None
+        L.ref_sample_batch.argtypes = [
+            C.POINTER(SamplerConfig), C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t,
+            C.POINTER(C.c_int32), C.c_int, C.c_size_t, C.POINTER(C.c_uint64),
+            C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+            C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int,
+        ]
+        L.ref_max_threads.restype = C.c_int
+        L.ref_sampler_sizeof.restype = C.c_int
+        L.ref_config_sizeof.restype = C.c_int
+        L.ref_init_state.restype = None
+        L.ref_init_state.argtypes = [C.POINTER(SamplerConfig), C.c_int, C.POINTER(C.c_uint64),
+                                     C.POINTER(SamplerConfig)]
+        # the reference ABI itself, for single-call known-answer tests
+        L.noel_sampler_sample.restype = C.c_int32
+        L.noel_sampler_random_f32.restype = C.c_float
+
+    @staticmethod
+    def available(path: str = REF_SO) -> bool:
+        return os.path.exists(path)
+
+    def max_threads(self) -> int:
+        return self.lib.ref_max_threads()
+
+    def sample_batch(self, cfg: SamplerConfig, logits: np.ndarray, vocab: int | None = None,
+                     history: np.ndarray | None = None, rng: np.ndarray | None = None,
+                     n_list: int = 0, nthreads: int = 0, in_place: bool = False) -> BatchResult:
+        B, ld = logits.shape
+        V = ld if vocab is None else vocab
+        if logits.dtype == np.uint16:  # bf16 bits: upcast exactly
+            logits = (logits.astype(np.uint32) << 16).view(np.float32)
+        lg = logits if in_place else np.ascontiguousarray(logits, dtype=np.float32)
+        rng = np.ascontiguousarray(rng.copy() if rng is not None else seed_states(np.arange(1, B + 1)),
+                                   dtype=np.uint64)
+        ids = np.empty(B, np.int32)
+        nc = np.empty(B, np.int32)
+        ci = np.empty((B, max(n_list, 1)), np.int32) if n_list else None
+        cv = np.empty((B, max(n_list, 1)), np.float32) if n_list else None
+        if history is not None:
+            history = np.ascontiguousarray(history, dtype=np.int32)
+            H, hld = history.shape[1], history.shape[1]
+        else:
+            H, hld = 0, 0
+        self.lib.ref_sample_batch(C.byref(cfg), _ptr(lg, C.c_float), B, V, ld,
+                                  _ptr(history, C.c_int32), H, hld, _ptr(rng, C.c_uint64),
+                                  _ptr(ids, C.c_int32), _ptr(nc, C.c_int32), _ptr(ci, C.c_int32),
+                                  _ptr(cv, C.c_float), n_list, 1 if in_place else 0, nthreads)
+        return BatchResult(ids=ids, rng=rng, num_cands=nc, topn_ids=ci, cand_vals=cv)
