@@ -1,0 +1,361 @@
+"""Throughput of the B200 token-sampling path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload batch1024] [--impl ours|reference]
+
+A step samples one batch of rows of the workload (default ``batch1024``:
+1024 rows x vocab 152,064 fp32 logits N(0, 2^2) with 8 ids +8.0 per row,
+history 64, repetition penalty 1.1, T 0.8, top-k 40, top-p 0.95) with the
+inputs resident in HBM.  N > 1 runs as one process per GPU under torchrun;
+every rank samples its own batch (batch sharding: no data-path collective),
+so ``value`` is the rows all ranks sampled per second and ``scaling`` is weak.
+
+Timing: W untimed steps, then K steps bracketed by a barrier and
+cudaDeviceSynchronize, measured with CUDA events on the launching stream,
+max over ranks.  The logits (623 MB per step) exceed the 126 MB L2, so no
+flush is needed between steps.  The single-pass kernel is also timed on its
+own (events around its launch) for the roofline; ``e2e`` is the same metric
+through the host-buffer C entry point (H2D of each step's rows from pinned
+memory, D2H of ids and states), and ``cpu_baseline`` is the reference's own
+sampler (oracle/_ref, compiled from its sources) on the box's host cores.
+
+``--impl reference`` times the reference CPU sampler alone on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sampled rows/s at batch 1024×vocab 152064 fp32; % of B200 HBM peak"
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(workload: str):
+    """DRAM bytes per launch of the single-pass kernel from the committed ncu
+    summary (line 'traffic_bytes_per_launch: N'), or None."""
+    p = os.path.join(ROOT, "profiles", f"sample_rows_kernel_{workload}.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def reduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def cpu_reference_rows_per_s(w, logits_host: np.ndarray, hist_host, rng_host, threads: int):
+    """The reference sampler (oracle/_ref) over the given rows; returns rows/s."""
+    from oracle.oracle import RefSampler, make_config
+
+    ref = RefSampler()
+    cfg = make_config(**w.config_kwargs())
+    ref.sample_batch(cfg, logits_host[: min(16, len(logits_host))], history=None if hist_host is None else
+                     hist_host[: min(16, len(logits_host))], rng=rng_host[: min(16, len(logits_host))],
+                     nthreads=threads)  # warm (page-in)
+    t0 = time.perf_counter()
+    ref.sample_batch(cfg, logits_host, history=hist_host, rng=rng_host, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return len(logits_host) / dt, dt
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU sampler on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from noel_b200.workloads import WORKLOADS, generate_numpy
+    from oracle.oracle import RefSampler
+
+    w = WORKLOADS[args.workload]
+    sample_rows = args.cpu_rows
+    d = generate_numpy(w, seed=1, rows=sample_rows)
+    threads = RefSampler().max_threads() if RefSampler.available() else os.cpu_count()
+    for _ in range(args.warmup):
+        cpu_reference_rows_per_s(w, d["logits"][:16], None if d["history"] is None else d["history"][:16],
+                                 d["rng"][:16], threads)
+    times = []
+    for _ in range(args.steps):
+        _, dt = cpu_reference_rows_per_s(w, d["logits"], d["history"], d["rng"], threads)
+        times.append(dt)
+    tot = sum(times)
+    value = sample_rows * len(times) / tot
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(w, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "reference",
+                         "sample": f"{sample_rows} rows of {w.name} per step (one noel_sampler_t per "
+                                   f"OpenMP thread, rows split across {threads} threads)"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    del torch
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(w, n_gpus):
+    return {"workload": w.name, "batch_per_gpu": w.batch, "global_batch": w.batch * n_gpus, "vocab": w.vocab,
+            "logits_dtype": w.dtype, "history": w.history, "temperature": w.temperature, "top_k": w.top_k,
+            "top_p": w.top_p, "repetition_penalty": w.repetition_penalty,
+            "parallelism": f"batch-sharded x{n_gpus}",
+            "l2": f"no flush: {w.batch * w.vocab * (4 if w.dtype == 'f32' else 2) / 1e6:.0f} MB of logits "
+                  f"per step > 126 MB L2"}
+
+
+def run_ours(args):
+    import torch
+
+    from noel_b200 import sampler as S
+    from noel_b200.workloads import WORKLOADS, generate_torch
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    w = WORKLOADS[args.workload]
+    d = generate_torch(w, dev, seed=1, row0=rank * w.batch)
+    logits, hist, rng = d["logits"], d["history"], d["rng"]
+    cfg = S.make_config(**w.config_kwargs())
+    B, V = logits.shape
+    ids = torch.empty(B, dtype=torch.int32, device=dev)
+    probs = torch.empty(B, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    dtype = S.F32 if logits.dtype == torch.float32 else S.BF16
+    hp, H, hld = (hist.data_ptr(), hist.shape[1], hist.stride(0)) if hist is not None else (None, 0, 0)
+
+    def step():
+        S.sample_batch_raw(cfg, logits.data_ptr(), dtype, B, V, logits.stride(0), hp, H, hld,
+                           rng.data_ptr(), ids.data_ptr(), probs.data_ptr(), stream.cuda_stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if args.profile:  # a short, allocation-light run for ncu captures
+        del d
+        torch.cuda.empty_cache()
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        return
+
+    # ---- timed region: whole steps ----
+    clocks = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    t_ms = e0.elapsed_time(e1)
+    t_ms = reduce_max(t_ms, world)
+    rows = B * world * args.steps
+    value = rows / (t_ms / 1e3)
+
+    # ---- the single-pass kernel alone (events around its launch) ----
+    kb = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ka = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        S.profile_events(kb[i], ka[i])
+        step()
+    S.profile_events(None, None)
+    torch.cuda.synchronize()
+    k_ms = float(np.mean([b.elapsed_time(a) for b, a in zip(kb, ka)]))
+    k_ms = reduce_max(k_ms, world)
+    peak, peak_kind = measured_peak()
+    bytes_per_launch = w.bytes_per_row() * B
+    achieved = bytes_per_launch / (k_ms / 1e3) / 1e9
+    traffic = profile_traffic(w.name)
+
+    # ---- end to end through the host-buffer C entry point ----
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    h_logits = logits.cpu().pin_memory()
+    h_hist = hist.cpu().pin_memory() if hist is not None else None
+    h_rng = rng.cpu().pin_memory()
+    lg_np = h_logits.view(torch.int16).numpy().view(np.uint16) if dtype == S.BF16 else h_logits.numpy()
+    hist_np = h_hist.numpy() if h_hist is not None else None
+    rng_np = h_rng.numpy().view(np.uint64)
+    S.sample_batch_host(cfg, lg_np, rng_np, history=hist_np)  # warm
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        S.sample_batch_host(cfg, lg_np, rng_np, history=hist_np)
+    e2e_s = reduce_max(time.perf_counter() - t0, world)
+    e2e_value = B * world * e2e_steps / e2e_s
+    h2d = lg_np.nbytes + (hist_np.nbytes if hist_np is not None else 0) + rng_np.nbytes
+    d2h = B * 4 + rng_np.nbytes
+
+    # ---- CPU baseline: the reference sampler on a bounded sample, rank 0 ----
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        from oracle.oracle import RefSampler
+
+        if RefSampler.available():
+            n = min(args.cpu_rows, B)
+            threads = RefSampler().max_threads()
+            rps, _ = cpu_reference_rows_per_s(w, lg_np[:n].copy() if dtype == S.F32 else
+                                              (lg_np[:n].astype(np.uint32) << 16).view(np.float32),
+                                              hist_np[:n].copy() if hist_np is not None else None,
+                                              rng_np[:n].copy(), threads)
+            cpu = {"value": rps, "unit": "rows/s", "cores": threads, "kind": "reference",
+                   "sample": f"{n} rows of {w.name} (one noel_sampler_t per OpenMP thread)"}
+        else:
+            cpu = {"value": None, "unit": "rows/s", "cores": 0, "kind": "reference",
+                   "sample": "oracle/_ref not built"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(w, world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "sample_rows_kernel", "kernel_ms": k_ms,
+                         "bytes_per_launch": bytes_per_launch, "peak_source": f"{peak_kind} hbm_gbs"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "api": "noel_sampler_sample_batch_host (pinned host buffers)"},
+            "clocks": clk,
+            "gpu_launches": 2 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="batch1024")
+    ap.add_argument("--cpu-rows", type=int, default=512)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="only W + K steps, for ncu")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -100,6 +100,14 @@ const char *noel_sampler_cuda_last_error_message(void);
 /* Static name of a status code. */
 const char *noel_sampler_cuda_status_string(int status);
 
+/*
+ * Profiling hook: record ev_before / ev_after (cudaEvent_t, or NULL to stop)
+ * on the launching stream around the single-pass sampling kernel of every
+ * later batched call made by this thread, so a caller can time that kernel
+ * alone with CUDA events.
+ */
+int noel_sampler_cuda_profile_events(void *ev_before, void *ev_after);
+
 /* Number of inputs x in (-15, 0] whose exp weight comes from the C-library
  * table rather than the correctly rounded exp (diagnostic). */
 int noel_sampler_cuda_expf_table_size(void);

@@ -132,6 +132,9 @@ int workspace(DeviceCtx *c, cudaStream_t s, int rows, int vocab, Workspace **out
     return NOEL_OK;
 }
 
+/* events recorded around the next main-kernel launches of this thread (profiling hook) */
+thread_local cudaEvent_t t_ev_before = nullptr, t_ev_after = nullptr;
+
 int set_smem(DeviceCtx *c, const void *kernel, size_t bytes) {
     std::lock_guard<std::mutex> lk(g_mu);
     size_t &cur = c->smem_set[kernel];
@@ -163,10 +166,12 @@ int launch_t(const SampleArgs &a0, int mode, size_t smem_main, size_t smem_exact
     if (r) return r;
     r = set_smem(c, kexact, smem_exact);
     if (r) return r;
+    if (t_ev_before) CUDA_TRY(cudaEventRecord(t_ev_before, s));
     if (mode == kGreedy) sample_rows_kernel<T, kGreedy><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
     else if (mode == kTopK) sample_rows_kernel<T, kTopK><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
     else sample_rows_kernel<T, kFullList><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
     CUDA_TRY(cudaGetLastError());
+    if (t_ev_after) CUDA_TRY(cudaEventRecord(t_ev_after, s));
     if (mode != kGreedy) {
         exact_rows_kernel<T><<<a0.nslots, kExactThreads, smem_exact, s>>>(a0);
         CUDA_TRY(cudaGetLastError());
@@ -579,6 +584,12 @@ extern "C" const char *noel_sampler_cuda_status_string(int status) {
 }
 
 extern "C" int noel_sampler_cuda_expf_table_size(void) { return NOEL_EXPF_NEXC; }
+
+extern "C" int noel_sampler_cuda_profile_events(void *ev_before, void *ev_after) {
+    t_ev_before = static_cast<cudaEvent_t>(ev_before);
+    t_ev_after = static_cast<cudaEvent_t>(ev_after);
+    return ok();
+}
 
 extern "C" int noel_sampler_cuda_expf_checksums(int chunk_log2, uint64_t *d_out, void *stream) {
     if (!d_out || chunk_log2 < 10 || chunk_log2 > 30) return fail(NOEL_ERR_INVALID_ARG, "chunk_log2 %d", chunk_log2);

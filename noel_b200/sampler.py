@@ -108,6 +108,8 @@ def lib() -> C.CDLL:
     L.noel_sampler_cuda_status_string.restype = C.c_char_p
     L.noel_sampler_cuda_status_string.argtypes = [C.c_int]
     L.noel_sampler_cuda_expf_table_size.restype = C.c_int
+    L.noel_sampler_cuda_profile_events.restype = C.c_int
+    L.noel_sampler_cuda_profile_events.argtypes = [C.c_void_p, C.c_void_p]
     L.noel_sampler_cuda_expf_checksums.restype = C.c_int
     L.noel_sampler_cuda_expf_checksums.argtypes = [C.c_int, C.c_void_p, C.c_void_p]
     _lib = L
@@ -259,6 +261,13 @@ def sample_batch_host(cfg: SamplerConfig, logits: np.ndarray, rng: np.ndarray, h
                                                 rng.ctypes.data, ids.ctypes.data,
                                                 pr.ctypes.data if pr is not None else None))
     return (ids, pr) if probs else ids
+
+
+def profile_events(before=None, after=None) -> None:
+    """Record torch.cuda.Event ``before``/``after`` around the single-pass
+    kernel of later batched calls on this thread (None, None to stop)."""
+    lib().noel_sampler_cuda_profile_events(before.cuda_event if before is not None else None,
+                                           after.cuda_event if after is not None else None)
 
 
 def expf_table_size() -> int:
