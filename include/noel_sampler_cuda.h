@@ -31,6 +31,7 @@ enum {
     NOEL_ERR_NO_DEVICE = -3,     /* no usable sm_100 device */
     NOEL_ERR_TOO_LARGE = -4,     /* size beyond what the entry point supports */
     NOEL_ERR_UNSUPPORTED = -5,   /* option combination not supported */
+    NOEL_ERR_DEVICE_WAIT = -6,   /* a kernel's bounded wait ran out; results of that call are invalid */
 };
 
 enum { NOEL_DTYPE_F32 = 0, NOEL_DTYPE_BF16 = 1 };
@@ -92,6 +93,14 @@ int noel_sampler_sample_batch_host(const noel_sampler_config_t *cfg, const void 
                                    int batch, int vocab, size_t ld, const int32_t *h_history,
                                    int history_len, size_t hld, uint64_t *h_rng, int32_t *h_ids,
                                    float *h_probs);
+
+/*
+ * Wait for the work queued on stream and report device-side failures of the
+ * batched calls made on it since the last check: NOEL_ERR_DEVICE_WAIT if a
+ * kernel's bounded wait for its row data ran out (the kernel then returns
+ * instead of hanging).  Clears the flag.
+ */
+int noel_sampler_cuda_sync_check(void *stream);
 
 /* Calling thread's last status (NOEL_OK after a successful call). */
 int noel_sampler_cuda_last_error(void);

@@ -177,10 +177,18 @@ NOEL_HD float noel_cr_expf(float x) {
  * glibc-identical expf on (-15, 0]: the correctly rounded value unless x is
  * in the exception table (keys sorted; bucket b holds keys
  * [offs[b], offs[b+1]) whose (bits - DOMAIN_FIRST) >> BUCKET_SHIFT == b).
+ * near: every exception has exp((double)x) within near double ulps of a float
+ * rounding midpoint (established by the table generator over all inputs);
+ * inputs farther away (with a margin for a 1-ulp difference between double
+ * exp implementations) skip the lookup.
  */
 NOEL_HD float noel_ref_expf(float x, const uint32_t *keys, const uint32_t *vals,
-                            const uint32_t *offs) {
-    const float y = noel_cr_expf(x);
+                            const uint32_t *offs, long long near = 0x10000000ll) {
+    const double d = exp((double)x);
+    const long long low = (long long)(noel_d2u(d) & 0x1FFFFFFFull) - 0x10000000ll;
+    const long long dist = low < 0 ? -low : low;
+    const float y = (dist < 64) ? noel_dd_to_float(noel_dd_exp(x)) : (float)d;
+    if (dist > near + 64) return y;
     const uint32_t k = noel_f2u(x) - NOEL_EXPF_DOMAIN_FIRST;
     if (keys && k < (NOEL_EXPF_DOMAIN_END - NOEL_EXPF_DOMAIN_FIRST)) {
         const uint32_t bkt = k >> NOEL_EXPF_BUCKET_SHIFT;

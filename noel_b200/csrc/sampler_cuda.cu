@@ -97,6 +97,7 @@ int device_ctx(DeviceCtx **out) {
         c.et.keys = static_cast<const uint32_t *>(k);
         c.et.vals = static_cast<const uint32_t *>(v);
         c.et.offs = static_cast<const uint32_t *>(o);
+        c.et.near = NOEL_EXPF_NEAR;
         c.ready = true;
     }
     *out = &c;
@@ -151,14 +152,16 @@ int pow2_at_least(int x) {
     return p;
 }
 
-constexpr int kMaxKprime = 1024;  // top-k mode up to k = 1016
+constexpr int kMaxKprime = 1024;     // top-k mode up to k = 1016
+constexpr int kWarpKprimeMax = 128;  // warp-streaming kernel up to k = 120
 constexpr int kCapMax = 4096;
 
 template <typename T>
-int launch_t(const SampleArgs &a0, int mode, size_t smem_main, size_t smem_exact, DeviceCtx *c,
+int launch_t(const SampleArgs &a0, int mode, bool block_kernel, size_t smem_main, size_t smem_exact, DeviceCtx *c,
              cudaStream_t s) {
     const void *kmain = nullptr;
-    if (mode == kGreedy) kmain = (const void *)sample_rows_kernel<T, kGreedy>;
+    if (block_kernel) kmain = (const void *)sample_rows_block_kernel<T, kTopK>;
+    else if (mode == kGreedy) kmain = (const void *)sample_rows_kernel<T, kGreedy>;
     else if (mode == kTopK) kmain = (const void *)sample_rows_kernel<T, kTopK>;
     else kmain = (const void *)sample_rows_kernel<T, kFullList>;
     const void *kexact = (const void *)exact_rows_kernel<T>;
@@ -167,9 +170,11 @@ int launch_t(const SampleArgs &a0, int mode, size_t smem_main, size_t smem_exact
     r = set_smem(c, kexact, smem_exact);
     if (r) return r;
     if (t_ev_before) CUDA_TRY(cudaEventRecord(t_ev_before, s));
-    if (mode == kGreedy) sample_rows_kernel<T, kGreedy><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
-    else if (mode == kTopK) sample_rows_kernel<T, kTopK><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
-    else sample_rows_kernel<T, kFullList><<<a0.batch, kMainThreads, smem_main, s>>>(a0);
+    const int grid = a0.batch;  // one CTA per row
+    if (block_kernel) sample_rows_block_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
+    else if (mode == kGreedy) sample_rows_kernel<T, kGreedy><<<grid, kMainThreads, smem_main, s>>>(a0);
+    else if (mode == kTopK) sample_rows_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
+    else sample_rows_kernel<T, kFullList><<<grid, kMainThreads, smem_main, s>>>(a0);
     CUDA_TRY(cudaGetLastError());
     if (t_ev_after) CUDA_TRY(cudaEventRecord(t_ev_after, s));
     if (mode != kGreedy) {
@@ -237,12 +242,20 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     if (T <= 1e-4f) mode = kGreedy;  // sampler.c:106
     else if (cfg->top_k > 0 && cfg->top_k <= kMaxKprime - 8) mode = kTopK;
     else mode = kFullList;
+    bool block_kernel = false;
     if (mode == kTopK) {
         a.kprime = pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
-        int cap = pow2_at_least(4 * a.kprime);
-        a.cap = cap < 512 ? 512 : (cap > kCapMax ? kCapMax : cap);
+        if (a.kprime <= kWarpKprimeMax) {
+            const int kw = a.kprime / 2 > 8 ? a.kprime / 2 : 8;  // kept per warp
+            const int cap = 4 * kw;                              // per-warp buffer
+            a.cap = cap < 64 ? 64 : cap;
+        } else {
+            block_kernel = true;
+            const int cap = pow2_at_least(4 * a.kprime);
+            a.cap = cap < 512 ? 512 : (cap > kCapMax ? kCapMax : cap);
+        }
     } else if (mode == kFullList) {
-        a.cap = kCapMax;
+        a.cap = 256;
     }
 
     size_t hist_bytes = 0;
@@ -252,13 +265,17 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         hist_bytes = (hist_bytes + 15) & ~size_t(15);
     }
     size_t smem_main = hist_bytes;
-    if (mode != kGreedy) smem_main += (size_t)a.cap * 8;
-    if (mode == kTopK) smem_main += kWarmBins * 4;
+    if (block_kernel) {
+        smem_main += (size_t)a.cap * 8 + kWarmBins * 4;
+    } else if (mode != kGreedy) {
+        const int nw = kMainThreads / 32;
+        smem_main += (size_t)nw * a.cap * 8 + (size_t)nw * 256 * 4 + (size_t)kUnionCap * 16;
+    }
     const size_t smem_exact = a.penalty && !a.wb ? hist_bytes : 0;
     if (smem_main > c->smem_optin - 2048 || smem_exact > c->smem_optin - 16384)
         return fail(NOEL_ERR_TOO_LARGE, "vocab %d / history %d need %zu B of shared memory", V, H, smem_main);
 
-    if (mode != kGreedy) {
+    {
         Workspace *w = nullptr;
         r = workspace(c, s, B, V, &w);
         if (r) return r;
@@ -267,8 +284,8 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         a.slots = w->slots;
         a.nslots = w->nslots;
     }
-    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, smem_main, smem_exact, c, s)
-                                : launch_t<uint16_t>(a, mode, smem_main, smem_exact, c, s);
+    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, block_kernel, smem_main, smem_exact, c, s)
+                                : launch_t<uint16_t>(a, mode, block_kernel, smem_main, smem_exact, c, s);
     if (r) return r;
     return ok();
 }
@@ -569,6 +586,28 @@ extern "C" int noel_sampler_sample_batch_host(const noel_sampler_config_t *cfg, 
     return ok();
 }
 
+extern "C" int noel_sampler_cuda_sync_check(void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    CUDA_TRY(cudaStreamSynchronize(s));
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    int32_t *flag = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = c->ws.find(s);
+        if (it != c->ws.end()) flag = it->second.counters + 3;
+    }
+    if (!flag) return ok();
+    int32_t v = 0;
+    CUDA_TRY(cudaMemcpy(&v, flag, sizeof(v), cudaMemcpyDeviceToHost));
+    if (v) {
+        CUDA_TRY(cudaMemset(flag, 0, sizeof(v)));
+        return fail(NOEL_ERR_DEVICE_WAIT, "a device-side wait ran out of its limit");
+    }
+    return ok();
+}
+
 extern "C" int noel_sampler_cuda_last_error(void) { return t_status; }
 extern "C" const char *noel_sampler_cuda_last_error_message(void) { return t_msg; }
 extern "C" const char *noel_sampler_cuda_status_string(int status) {
@@ -579,6 +618,7 @@ extern "C" const char *noel_sampler_cuda_status_string(int status) {
         case NOEL_ERR_NO_DEVICE: return "no usable device";
         case NOEL_ERR_TOO_LARGE: return "size too large";
         case NOEL_ERR_UNSUPPORTED: return "unsupported option";
+        case NOEL_ERR_DEVICE_WAIT: return "device-side wait ran out";
         default: return "unknown status";
     }
 }

@@ -51,6 +51,7 @@ enum { kTruncated = 1, kOverflow = 2, kNeedExact = 4 };
 
 struct ExpTable {
     const uint32_t *keys, *vals, *offs;
+    long long near;  // exceptions lie within this many double ulps of a midpoint
 };
 
 /* Kernel arguments (by value). */
@@ -120,7 +121,7 @@ __device__ __forceinline__ float scaled_diff(float x, float m, float inv_t) {
 }
 
 __device__ __forceinline__ float ref_weight(float d, const ExpTable &et) {
-    return noel_ref_expf(d, et.keys, et.vals, et.offs);
+    return noel_ref_expf(d, et.keys, et.vals, et.offs, et.near);
 }
 
 /* ---------------------------------------------------------------------- */
@@ -261,6 +262,20 @@ __device__ __forceinline__ uint32_t hist_bits(const HistView &h, int id0, int n)
     return b & ((1u << n) - 1u);
 }
 
+/* the penalty for the group of N consecutive ids starting at id0 */
+template <int N>
+__device__ __forceinline__ void penalize_group(const HistView &hv, int id0, float *x, float rep) {
+    uint32_t bits = hist_bits(hv, id0, N);
+    while (bits) {
+        const int j = __ffs(bits) - 1;
+        bits &= bits - 1;
+        const uint32_t c = hv.cnt[hist_rank(hv, id0 + j)];
+#pragma unroll
+        for (int jj = 0; jj < N; ++jj)
+            if (jj == j) x[jj] = apply_penalty(x[jj], c, rep);
+    }
+}
+
 /* ---------------------------------------------------------------------- */
 /* element formats                                                          */
 
@@ -306,6 +321,52 @@ __device__ __forceinline__ V8 ld_stream(const V8 *p) {
           "=r"(r.v[6]), "=r"(r.v[7])
         : "l"(p));
     return r;
+}
+
+/* ---------------------------------------------------------------------- */
+/* 1-D bulk copies (TMA) into shared memory, completed on an mbarrier       */
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+/* order earlier generic-proxy reads of a stage before the async-proxy write that reuses it */
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+/* global -> shared, bytes a multiple of 16, both addresses 16-byte aligned; no multicast */
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+/* bounded wait: false after kWaitTries unsuccessful polls (each poll may
+ * suspend the thread for a while), so a lost copy ends as an error, not a hang */
+constexpr uint32_t kWaitTries = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitTries; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
 }
 
 /* Row geometry: scalar head until 32-byte alignment, vector body, scalar tail. */
@@ -542,5 +603,296 @@ __device__ __forceinline__ TailOut run_tail(int num_cands, bool more_than_listed
     }
     return o;
 }
+
+}  // namespace noel
+
+namespace noel {
+
+/* ---------------------------------------------------------------------- */
+/* warp-level candidate buffer primitives (no block barriers)              */
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+    return (1u << (threadIdx.x & 31)) - 1u;
+}
+
+/* digit d (searching from the top when desc) whose cumulative count crosses need */
+__device__ __forceinline__ void warp_find_digit(const uint32_t *hist, int need, bool desc, int &digit,
+                                                int &before_cnt, int &eq) {
+    const int lane = threadIdx.x & 31;
+    int c[8], s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        c[j] = (int)hist[desc ? 255 - 8 * lane - j : 8 * lane + j];
+        s += c[j];
+    }
+    const int inc = warp_incl_scan(s);
+    const int before = inc - s;
+    const uint32_t sel = __ballot_sync(kFull, before < need && need <= inc);
+    const int src = sel ? __ffs(sel) - 1 : 31;
+    int d = 0, ab = 0, e = 0;
+    if (lane == src) {
+        int cum = before;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (cum < need && need <= cum + c[j] && e == 0) {
+                d = desc ? 255 - 8 * lane - j : 8 * lane + j;
+                ab = cum;
+                e = c[j];
+            }
+            cum += c[j];
+        }
+    }
+    digit = __shfl_sync(kFull, d, src);
+    before_cnt = __shfl_sync(kFull, ab, src);
+    eq = __shfl_sync(kFull, e, src);
+}
+
+/*
+ * 256-bin histogram of digit (v >> shift) & 255 over the entries whose value
+ * matches prefix under mask (and, if sel_key is given, whose sel_key equals
+ * sel).  Equal digits within a warp-wide batch are counted once by their
+ * leader (match_any), so heavily repeated digits do not serialise atomics.
+ */
+__device__ __forceinline__ void warp_digit_hist(uint32_t *hist, const uint32_t *v, const uint32_t *sel_key,
+                                                uint32_t sel, int n, uint32_t mask, uint32_t prefix, int shift) {
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < 256; i += 32) hist[i] = 0u;
+    __syncwarp();
+    for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        bool ok = i < n;
+        uint32_t x = 0u;
+        if (ok) {
+            x = v[i];
+            ok = (x & mask) == prefix && (sel_key == nullptr || sel_key[i] == sel);
+        }
+        const uint32_t d = ok ? (x >> shift) & 255u : 256u + lane;  // unique tag when not counted
+        const uint32_t peers = __match_any_sync(kFull, d);
+        if (ok && (peers & lanemask_lt()) == 0u) hist[d] += (uint32_t)__popc(peers);
+        __syncwarp();
+    }
+}
+
+/*
+ * Keep the K largest of n (K <= n) entries by (key desc, id asc), compacted
+ * in place (stable) into [0, K).  Returns the K-th key; *ithr = largest kept id
+ * among entries with that key when ties were cut, else 0xFFFFFFFF.
+ * hist: 256 words of this warp's shared memory.
+ */
+__device__ uint32_t warp_select_top(uint32_t *key, uint32_t *id, int n, int K, uint32_t *hist, uint32_t *ithr) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0, mask = 0;
+    int need = K, eq = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        warp_digit_hist(hist, key, nullptr, 0u, n, mask, prefix, shift);
+        int d, before;
+        warp_find_digit(hist, need, true, d, before, eq);
+        prefix |= (uint32_t)d << shift;
+        mask |= 0xFFu << shift;
+        need -= before;
+        __syncwarp();
+    }
+    const uint32_t t = prefix;
+    uint32_t it = 0xFFFFFFFFu;
+    if (eq > need) {
+        uint32_t ip = 0, im = 0;
+        int need2 = need, eq2;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            warp_digit_hist(hist, id, key, t, n, im, ip, shift);
+            int d, before;
+            warp_find_digit(hist, need2, false, d, before, eq2);
+            ip |= (uint32_t)d << shift;
+            im |= 0xFFu << shift;
+            need2 -= before;
+            __syncwarp();
+        }
+        it = ip;
+    }
+    int w = 0;
+    for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        const bool ok = i < n;
+        const uint32_t k = ok ? key[i] : 0u, v = ok ? id[i] : 0u;
+        const bool keep = ok && (k > t || (k == t && v <= it));
+        const uint32_t b = __ballot_sync(kFull, keep);
+        __syncwarp();
+        if (keep) {
+            const int pos = w + __popc(b & lanemask_lt());
+            key[pos] = k;
+            id[pos] = v;
+        }
+        w += __popc(b);
+        __syncwarp();
+    }
+    *ithr = it;
+    return t;
+}
+
+/* keep entries passing the -15 cut under max m (sampler.c:137-138); returns the count */
+__device__ int warp_filter_by_max(uint32_t *key, uint32_t *id, int n, float m, float inv_t) {
+    const int lane = threadIdx.x & 31;
+    int w = 0;
+    for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        const bool ok = i < n;
+        const uint32_t k = ok ? key[i] : 0u, v = ok ? id[i] : 0u;
+        const bool keep = ok && scaled_diff(key_float(k), m, inv_t) > -15.0f;
+        const uint32_t b = __ballot_sync(kFull, keep);
+        __syncwarp();
+        if (keep) {
+            const int pos = w + __popc(b & lanemask_lt());
+            key[pos] = k;
+            id[pos] = v;
+        }
+        w += __popc(b);
+        __syncwarp();
+    }
+    return w;
+}
+
+/* descending bitonic sort of P (power of two) 64-bit keys by one warp */
+__device__ void warp_bitonic_desc(uint64_t *a, int P) {
+    const int lane = threadIdx.x & 31;
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < P; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t ai = a[i], aj = a[ixj];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (ai < aj) : (ai > aj)) {
+                        a[i] = aj;
+                        a[ixj] = ai;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+__device__ __forceinline__ uint32_t warp_max_u(uint32_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_min_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+}  // namespace noel
+
+namespace noel {
+
+/* ---------------------------------------------------------------------- */
+/* register-resident warp sort of 32*R 64-bit keys                         */
+
+/* Descending bitonic sort; element i = lane*R + r is k[r] of lane i/R. */
+template <int R>
+__device__ __forceinline__ void warp_sort_desc(uint64_t (&k)[R]) {
+    const int lane = threadIdx.x & 31;
+    constexpr int N = 32 * R;
+#pragma unroll
+    for (int kk = 2; kk <= N; kk <<= 1) {
+#pragma unroll
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+            if (j >= R) {
+                const int lj = j / R;
+                const bool lower = (lane & lj) == 0;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int i = lane * R + r;
+                    const uint64_t o = __shfl_xor_sync(kFull, k[r], lj);
+                    const bool desc = (i & kk) == 0;
+                    k[r] = (desc == lower) ? (k[r] > o ? k[r] : o) : (k[r] < o ? k[r] : o);
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int rp = r ^ j;
+                    if (rp > r) {
+                        const int i = lane * R + r;
+                        const bool desc = (i & kk) == 0;
+                        const uint64_t a = k[r], b = k[rp];
+                        const bool sw = desc ? (a < b) : (a > b);
+                        k[r] = sw ? b : a;
+                        k[rp] = sw ? a : b;
+                    }
+                }
+            }
+        }
+    }
+}
+
+/* (key desc, id asc) as one 64-bit key: larger is better */
+__device__ __forceinline__ uint64_t comp_key(uint32_t key, uint32_t id) {
+    return ((uint64_t)key << 32) | (uint64_t)(0xFFFFFFFFu - id);
+}
+
+/*
+ * Top-K of n entries (key[], id[]) by (key desc, id asc) with a running
+ * register sort of 32*R at a time (the best K so far plus the next 32*R-K
+ * entries; K < 32*R).  Entries are read and written at r*32 + lane
+ * (conflict-free); the sort runs on the lane-major order (input order is
+ * irrelevant to a selection).  The kept entries are written back sorted to
+ * [0, min(n, K)), and ladder[0..2] receive the composite keys
+ * at sorted positions K/4-1, K/2-1 and K-1.  Returns the K-th composite
+ * key (0 if n < K); the kept count is min(n, K).  Out of line: it runs
+ * rarely and its unrolled network would otherwise crowd the streaming loop.
+ */
+template <int R>
+__device__ __noinline__ uint64_t warp_topk_sorted_r(uint32_t *key, uint32_t *id, int n, int K, uint64_t *ladder) {
+    constexpr int N = 32 * R;
+    const int lane = threadIdx.x & 31;
+    uint64_t k[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int i = r * 32 + lane;
+        k[r] = i < n ? comp_key(key[i], id[i]) : 0ull;
+    }
+    warp_sort_desc<R>(k);
+    for (int next = N; next < n; next += N - K) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int p = lane * R + r;  // sorted position held here
+            if (p >= K) {
+                const int src = next + (p - K);
+                k[r] = src < n ? comp_key(key[src], id[src]) : 0ull;
+            }
+        }
+        warp_sort_desc<R>(k);
+    }
+    __syncwarp();
+    uint64_t l0 = 0ull, l1 = 0ull, l2 = 0ull;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int p = lane * R + r;
+        if (p < K && p < n) {  // kept entries, contiguous and sorted
+            key[p] = (uint32_t)(k[r] >> 32);
+            id[p] = 0xFFFFFFFFu - (uint32_t)k[r];
+        }
+        if (p == K / 4 - 1) l0 = k[r];
+        if (p == K / 2 - 1) l1 = k[r];
+        if (p == K - 1) l2 = k[r];
+    }
+    l0 = __shfl_sync(kFull, l0, (K / 4 - 1) / R);
+    l1 = __shfl_sync(kFull, l1, (K / 2 - 1) / R);
+    l2 = __shfl_sync(kFull, l2, (K - 1) / R);
+    if (ladder) {
+        ladder[0] = l0;
+        ladder[1] = l1;
+        ladder[2] = l2;
+    }
+    __syncwarp();
+    return n >= K ? l2 : 0ull;
+}
+
 
 }  // namespace noel

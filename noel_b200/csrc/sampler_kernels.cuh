@@ -9,6 +9,8 @@
 namespace noel {
 
 constexpr int kMainThreads = 256;
+constexpr int kStages = 8;        // shared-memory ring stages per CTA
+constexpr int kChunk = 8192;       // bytes per stage (one bulk copy)
 constexpr int kEPT = 16;         // buffer entries per thread in compactions (cap <= 4096)
 constexpr int kWarmBins = 2048;  // warm-up histogram on the top 11 key bits
 constexpr int kExactThreads = 256;
@@ -51,10 +53,10 @@ __device__ __forceinline__ void list_exact_row(const SampleArgs &a, int row) {
 }
 
 /* ====================================================================== */
-/* main kernel: one CTA per row                                            */
+/* block-level kernel for large kept sets (k > 120): one CTA per row       */
 
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kMainThreads, 4) sample_rows_kernel(const SampleArgs a) {
+__global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(const SampleArgs a) {
     using F = Fmt<T>;
     constexpr int NT = kMainThreads;
     constexpr int VEC = F::VEC, U = F::U, NE = U * VEC;
@@ -507,6 +509,12 @@ __global__ void __launch_bounds__(kMainThreads, 4) sample_rows_kernel(const Samp
         }
     }
 }
+
+}  // namespace noel
+
+#include "sampler_warp.cuh"
+
+namespace noel {
 
 /* ====================================================================== */
 /* exact two-pass kernel for listed rows                                   */

@@ -266,6 +266,9 @@ def sample_batch_host(cfg: SamplerConfig, logits: np.ndarray, rng: np.ndarray, h
 def profile_events(before=None, after=None) -> None:
     """Record torch.cuda.Event ``before``/``after`` around the single-pass
     kernel of later batched calls on this thread (None, None to stop)."""
+    for ev in (before, after):
+        if ev is not None and not ev.cuda_event:
+            ev.record()  # torch creates the CUDA event on its first record
     lib().noel_sampler_cuda_profile_events(before.cuda_event if before is not None else None,
                                            after.cuda_event if after is not None else None)
 
