@@ -172,9 +172,9 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, size_t smem_main
     if (t_ev_before) CUDA_TRY(cudaEventRecord(t_ev_before, s));
     const int grid = a0.batch;  // one CTA per row
     if (block_kernel) sample_rows_block_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
-    else if (mode == kGreedy) sample_rows_kernel<T, kGreedy><<<grid, kMainThreads, smem_main, s>>>(a0);
-    else if (mode == kTopK) sample_rows_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
-    else sample_rows_kernel<T, kFullList><<<grid, kMainThreads, smem_main, s>>>(a0);
+    else if (mode == kGreedy) sample_rows_kernel<T, kGreedy><<<grid, kRowThreads, smem_main, s>>>(a0);
+    else if (mode == kTopK) sample_rows_kernel<T, kTopK><<<grid, kRowThreads, smem_main, s>>>(a0);
+    else sample_rows_kernel<T, kFullList><<<grid, kRowThreads, smem_main, s>>>(a0);
     CUDA_TRY(cudaGetLastError());
     if (t_ev_after) CUDA_TRY(cudaEventRecord(t_ev_after, s));
     if (mode != kGreedy) {
@@ -268,7 +268,7 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     if (block_kernel) {
         smem_main += (size_t)a.cap * 8 + kWarmBins * 4;
     } else if (mode != kGreedy) {
-        const int nw = kMainThreads / 32;
+        const int nw = kRowWarps;
         smem_main += (size_t)nw * a.cap * 8 + (size_t)nw * 256 * 4 + (size_t)kUnionCap * 16;
     }
     const size_t smem_exact = a.penalty && !a.wb ? hist_bytes : 0;

@@ -843,12 +843,13 @@ __device__ __forceinline__ uint64_t comp_key(uint32_t key, uint32_t id) {
  * (conflict-free); the sort runs on the lane-major order (input order is
  * irrelevant to a selection).  The kept entries are written back sorted to
  * [0, min(n, K)), and ladder[0..2] receive the composite keys
- * at sorted positions K/4-1, K/2-1 and K-1.  Returns the K-th composite
+ * at sorted positions lad0-1, K/2-1 and K-1.  Returns the K-th composite
  * key (0 if n < K); the kept count is min(n, K).  Out of line: it runs
  * rarely and its unrolled network would otherwise crowd the streaming loop.
  */
 template <int R>
-__device__ __noinline__ uint64_t warp_topk_sorted_r(uint32_t *key, uint32_t *id, int n, int K, uint64_t *ladder) {
+__device__ __noinline__ uint64_t warp_topk_sorted_r(uint32_t *key, uint32_t *id, int n, int K, uint64_t *ladder,
+                                                   int lad0) {
     constexpr int N = 32 * R;
     const int lane = threadIdx.x & 31;
     uint64_t k[R];
@@ -878,11 +879,11 @@ __device__ __noinline__ uint64_t warp_topk_sorted_r(uint32_t *key, uint32_t *id,
             key[p] = (uint32_t)(k[r] >> 32);
             id[p] = 0xFFFFFFFFu - (uint32_t)k[r];
         }
-        if (p == K / 4 - 1) l0 = k[r];
+        if (p == lad0 - 1) l0 = k[r];
         if (p == K / 2 - 1) l1 = k[r];
         if (p == K - 1) l2 = k[r];
     }
-    l0 = __shfl_sync(kFull, l0, (K / 4 - 1) / R);
+    l0 = __shfl_sync(kFull, l0, (lad0 - 1) / R);
     l1 = __shfl_sync(kFull, l1, (K / 2 - 1) / R);
     l2 = __shfl_sync(kFull, l2, (K - 1) / R);
     if (ladder) {

@@ -26,18 +26,55 @@
 namespace noel {
 
 constexpr int kUnionCap = 1024;  // row-end gather / sort area (entries)
+constexpr int kRowWarps = 4;     // warps streaming one row
+constexpr int kRowThreads = 32 * kRowWarps;
+
+/* Bin of the K-th largest count in a 2048-bin histogram (counted from the top
+ * bin down), found by all NT threads: each owns 2048/NT consecutive bins.
+ * Returns the bin (or -1 if the total is below K); *need_in_bin = how many of
+ * that bin's entries are needed. */
+template <int NT>
+__device__ int block_find_bin_desc(const uint32_t *h, int K, int *s_w, int *s_res, int *need_in_bin) {
+    constexpr int PER = 2048 / NT;
+    const int hi = 2047 - threadIdx.x * PER;  // this thread's bins: hi, hi-1, ..., hi-PER+1
+    int c[PER], sum = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        c[j] = (int)h[hi - j];
+        sum += c[j];
+    }
+    int total;
+    const int before = block_excl_scan<NT>(sum, s_w, total);
+    if (threadIdx.x == 0) s_res[0] = -1;
+    __syncthreads();
+    if (before < K && K <= before + sum) {
+        int cum = before;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            if (cum < K && K <= cum + c[j]) {
+                s_res[0] = hi - j;
+                s_res[1] = K - cum;
+            }
+            cum += c[j];
+        }
+    }
+    __syncthreads();
+    *need_in_bin = s_res[1];
+    return s_res[0];
+}
 
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const SampleArgs a) {
+__global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kernel(const SampleArgs a) {
     using F = Fmt<T>;
-    constexpr int NT = kMainThreads, NW = NT / 32;
+    constexpr int NT = kRowThreads, NW = NT / 32;
     constexpr int VEC = F::VEC, U = F::U, NE = U * VEC;
     static_assert(NE <= 32, "pending mask is 32 bits");
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ unsigned long long s_taus[NW];  // each warp's own exclusion threshold
     __shared__ unsigned long long s_btau;      // block warm-up threshold (top-k)
     __shared__ unsigned long long s_tsh;       // best shared filter (warm-up or ladders)
-    __shared__ unsigned long long s_lad[3][NW];  // each warp's kw/4-th, kw/2-th, kw-th kept key
+    __shared__ unsigned long long s_lad[3][NW];  // each warp's (2kw/NW)-th, (kw/2)-th, kw-th kept key
+    __shared__ int s_res[2];
     __shared__ uint32_t s_maxkey;
     __shared__ int s_flags, s_l0nan, s_trunc;
     __shared__ int s_wcnt[NW];
@@ -200,29 +237,8 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
         __syncthreads();
         /* level 1: bin (top 11 key bits) of the K'-th largest; level 2: the next
          * 11 bits inside that bin */
-        __shared__ int s_wb, s_wneed;
-        if (warp == 0) {
-            int sum = 0;
-            for (int j = 0; j < 64; ++j) sum += (int)ukey[2047 - lane * 64 - j];
-            const int inc = warp_incl_scan(sum);
-            const int before = inc - sum;
-            if (lane == 0) s_wb = -1;
-            __syncwarp();
-            if (before < a.kprime && a.kprime <= inc) {
-                int cum = before;
-                for (int j = 0; j < 64; ++j) {
-                    const int b = 2047 - lane * 64 - j;
-                    if (cum + (int)ukey[b] >= a.kprime) {
-                        s_wb = b;
-                        s_wneed = a.kprime - cum;
-                        break;
-                    }
-                    cum += (int)ukey[b];
-                }
-            }
-        }
-        __syncthreads();
-        const int wb = s_wb;
+        int need;
+        const int wb = block_find_bin_desc<NT>(ukey, a.kprime, s_w, s_res, &need);
         if (wb >= 0) {
             uint32_t *h2 = ukey + 2048;  // second-level bins
             for (int i = tid; i < 2048; i += NT) h2[i] = 0u;
@@ -234,25 +250,12 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
                     atomicAdd(&h2[(ord_key(xv) >> 10) & 2047u], 1u);
             }
             __syncthreads();
-            if (warp == 0) {
-                const int need = s_wneed;
-                int sum = 0;
-                for (int j = 0; j < 64; ++j) sum += (int)h2[2047 - lane * 64 - j];
-                const int inc = warp_incl_scan(sum);
-                const int before = inc - sum;
-                if (before < need && need <= inc) {
-                    int cum = before;
-                    for (int j = 0; j < 64; ++j) {
-                        const int b = 2047 - lane * 64 - j;
-                        cum += (int)h2[b];
-                        if (cum >= need) {
-                            const uint32_t key = ((uint32_t)wb << 21) | ((uint32_t)b << 10);
-                            s_btau = (unsigned long long)key << 32;
-                            s_tsh = s_btau;
-                            break;
-                        }
-                    }
-                }
+            int need2;
+            const int b2 = block_find_bin_desc<NT>(h2, need, s_w, s_res, &need2);
+            if (tid == 0 && b2 >= 0) {
+                const uint32_t key = ((uint32_t)wb << 21) | ((uint32_t)b2 << 10);
+                s_btau = (unsigned long long)key << 32;
+                s_tsh = s_btau;
             }
             __syncthreads();
         }
@@ -386,23 +389,19 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
             if (!__any_sync(kFull, pend != 0u)) break;
             if (pend) {
                 int slot = atomicAdd(&s_wfill[warp], __popc(pend));
+                uint32_t pp = pend;
+                while (pp) {  // compact loop: this path is rare
+                    const int e = __ffs(pp) - 1;
+                    pp &= pp - 1;
+                    if (slot < capw) {
+                        float xv = x[0];
 #pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    if ((pend >> (u * VEC)) & ((1u << VEC) - 1u)) {
-                        const uint32_t id0 = (uint32_t)(g.head + (base + u * 32 + lane) * VEC);
-#pragma unroll
-                        for (int j = 0; j < VEC; ++j) {
-                            const int e = u * VEC + j;
-                            if ((pend >> e) & 1u) {
-                                if (slot < capw) {
-                                    wkey[slot] = ord_key(x[e]);
-                                    wid[slot] = id0 + j;
-                                    pend &= ~(1u << e);
-                                }
-                                ++slot;
-                            }
-                        }
+                        for (int q = 1; q < NE; ++q) xv = (q == e) ? x[q] : xv;
+                        wkey[slot] = ord_key(xv);
+                        wid[slot] = (uint32_t)(g.head + (base + (e / VEC) * 32 + lane) * VEC + (e % VEC));
+                        pend &= ~(1u << e);
                     }
+                    ++slot;
                 }
             }
             if (!__any_sync(kFull, pend != 0u)) break;
@@ -411,7 +410,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
             __syncwarp();
             if (MODE == kTopK) {
                 uint64_t lad[3];
-                tau_w = warp_topk_sorted_r<4>(wkey, wid, wcount, kw, lad);
+                tau_w = warp_topk_sorted_r<4>(wkey, wid, wcount, kw, lad, max(1, 2 * kw / NW));
                 wcount = kw;
                 wtrunc = true;
                 if (lane == 0) {
@@ -421,8 +420,9 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
                     s_lad[1][warp] = lad[1];
                     s_lad[2][warp] = lad[2];
                     __threadfence_block();
-                    /* K' retained elements beat each of: every warp's kw/4-th,
-                     * the 4th largest kw/2-th, the 2nd largest kw-th */
+                    /* K' retained elements beat each of: every warp's
+                     * (2kw/NW)-th, the 4th largest (kw/2)-th (NW >= 4), the
+                     * 2nd largest kw-th */
                     unsigned long long mn = ~0ull, b[4] = {0ull, 0ull, 0ull, 0ull}, c1 = 0ull, c2 = 0ull;
                     for (int w = 0; w < NW; ++w) {
                         const unsigned long long l0 = *(volatile unsigned long long *)&s_lad[0][w];
@@ -437,6 +437,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
                             }
                         if (l2 > c1) { c2 = c1; c1 = l2; } else if (l2 > c2) { c2 = l2; }
                     }
+                    if (NW < 4) b[3] = 0ull;
                     atomicMax(&s_tsh, max(max(mn, b[3]), c2));
                 }
                 tau_eff = max(tau_w, *(volatile unsigned long long *)&s_tsh);
@@ -537,7 +538,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
             wcount = wn;
         }
         if (wcount > 2 * kw) {  // keeps the gather within its area
-            tau_w = warp_topk_sorted_r<4>(wkey, wid, wcount, kw, nullptr);
+            tau_w = warp_topk_sorted_r<4>(wkey, wid, wcount, kw, nullptr, 1);
             wcount = kw;
             wtrunc = true;
         }
@@ -578,8 +579,8 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_kernel(const Samp
         for (int w = 0; w < NW; ++w) worst = max(worst, s_taus[w]);
         const unsigned long long T =
             n < a.kprime ? 0ull
-                         : (a.kprime < 128 ? warp_topk_sorted_r<4>(ukey, uid, n, a.kprime, nullptr)
-                                           : warp_topk_sorted_r<8>(ukey, uid, n, a.kprime, nullptr));
+                         : (a.kprime < 128 ? warp_topk_sorted_r<4>(ukey, uid, n, a.kprime, nullptr, 1)
+                                           : warp_topk_sorted_r<8>(ukey, uid, n, a.kprime, nullptr, 1));
         if (n < a.kprime || !(T > worst)) {
             if (lane == 0) list_exact_row(a, row);
             return;
