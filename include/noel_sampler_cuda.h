@@ -83,6 +83,28 @@ int noel_sampler_sample_batch_ex(const noel_sampler_config_t *cfg, const void *d
                                  const noel_sample_extras_t *extras, void *stream);
 
 /*
+ * noel_sampler_sample_batch for callers that cannot allocate device memory.
+ * No counterpart in the reference.  Some callers can't call cudaMalloc: a
+ * serving loop that fixed its device-memory budget at start-up and must not
+ * grow it (or risk cudaMalloc synchronising the device mid-stream), or an
+ * embedding application whose allocator owns all device memory and gives the
+ * sampler none.  This entry point allocates nothing: the scratch of the
+ * two-pass kernel lives in a static device array of the library image
+ * (8,421,632 bytes, held by every GPU that loads the library until exit).
+ * Limits: batch <= 8192 rows, vocab <= 262144; larger calls return
+ * NOEL_ERR_TOO_LARGE.  The first call on each device does a one-time set-up
+ * (looks up the array's device address and sets kernel attributes) and should
+ * come before any stream capture.  All calls share the array and it keeps the
+ * last call's contents (the call clears what must start empty), so calls that
+ * overlap on one GPU (issued on different streams) race: issue them on one
+ * stream per device.  Arguments as noel_sampler_sample_batch.
+ */
+int noel_sampler_sample_batch_noalloc(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
+                                      int batch, int vocab, size_t ld, const int32_t *d_history,
+                                      int history_len, size_t hld, uint64_t *d_rng, int32_t *d_ids,
+                                      float *d_probs, void *stream);
+
+/*
  * Host-buffer form of noel_sampler_sample_batch for callers whose logits are
  * in host memory (the reference engine's layout, src/engine.c:59): copies the
  * rows, histories and states to the device, samples, and copies ids, states

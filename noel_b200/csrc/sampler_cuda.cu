@@ -186,7 +186,7 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, size_t smem_main
 
 int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype, int B, int V,
                  size_t ld, const int32_t *hist, int H, size_t hld, uint64_t *rng, int32_t *ids,
-                 const noel_sample_extras_t *ex, cudaStream_t s) {
+                 const noel_sample_extras_t *ex, cudaStream_t s, const Workspace *fixed_ws = nullptr) {
     if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
     if (B < 0 || V <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", B, V);
     if (B == 0) return ok();
@@ -275,7 +275,12 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     if (smem_main > c->smem_optin - 2048 || smem_exact > c->smem_optin - 16384)
         return fail(NOEL_ERR_TOO_LARGE, "vocab %d / history %d need %zu B of shared memory", V, H, smem_main);
 
-    {
+    if (fixed_ws) {  // caller-provided scratch (the allocation-free entry point)
+        a.counters = fixed_ws->counters;
+        a.exact_list = fixed_ws->rows;
+        a.slots = fixed_ws->slots;
+        a.nslots = fixed_ws->nslots;
+    } else {
         Workspace *w = nullptr;
         r = workspace(c, s, B, V, &w);
         if (r) return r;
@@ -644,4 +649,101 @@ extern "C" int noel_sampler_cuda_expf_checksums(int chunk_log2, uint64_t *d_out,
     expf_checksum_kernel<<<grid, 256, 0, s>>>(chunk_log2, d_out, c->et);
     CUDA_TRY(cudaGetLastError());
     return ok();
+}
+
+/* ========================================================================= */
+/* allocation-free entry point                                                */
+
+namespace {
+
+/*
+ * Scratch of noel_sampler_sample_batch_noalloc, held in the library's device
+ * image: every GPU that loads the library keeps these kNoAllocBytes
+ * (8,421,632 B) until the process exits.  Layout: 4 counters (padded to
+ * 256 B), the row list of the two-pass kernel (kNoAllocMaxRows int32), and
+ * kNoAllocSlots candidate slots of 2 x kNoAllocMaxVocab (x, id) pairs.
+ */
+constexpr int kNoAllocMaxRows = 8192;
+constexpr int kNoAllocMaxVocab = 262144;
+constexpr int kNoAllocSlots = 2;
+constexpr size_t kNoAllocRowsOff = 256;
+constexpr size_t kNoAllocSlotsOff = kNoAllocRowsOff + (size_t)kNoAllocMaxRows * sizeof(int32_t);
+constexpr size_t kNoAllocBytes = kNoAllocSlotsOff + (size_t)kNoAllocSlots * 2 * kNoAllocMaxVocab * sizeof(uint2);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+struct NoAllocDev {
+    bool ready = false;
+    Workspace ws;
+};
+std::mutex g_noalloc_mu;
+NoAllocDev g_noalloc_dev[64];  // per device ordinal; fixed storage, nothing allocated per call
+
+template <typename T>
+int preset_attrs(DeviceCtx *c) {
+    const size_t mx = c->smem_optin;
+    const void *ks[] = {(const void *)sample_rows_kernel<T, kGreedy>, (const void *)sample_rows_kernel<T, kTopK>,
+                        (const void *)sample_rows_kernel<T, kFullList>, (const void *)sample_rows_block_kernel<T, kTopK>,
+                        (const void *)exact_rows_kernel<T>};
+    for (const void *k : ks) {
+        cudaFuncAttributes fa;
+        CUDA_TRY(cudaFuncGetAttributes(&fa, k));
+        int r = set_smem(c, k, mx - fa.sharedSizeBytes);  // dynamic limit: opt-in minus static
+        if (r) return r;
+    }
+    return NOEL_OK;
+}
+
+/* once per device, with that device current: the scratch's device address */
+int noalloc_setup(int dev, DeviceCtx *c, const Workspace **out) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocDev &d = g_noalloc_dev[dev];
+    if (!d.ready) {
+        void *base = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&base, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(NOEL_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+        int r = preset_attrs<float>(c);
+        if (!r) r = preset_attrs<uint16_t>(c);
+        if (r) return r;
+        unsigned char *b = static_cast<unsigned char *>(base);
+        d.ws.counters = reinterpret_cast<int32_t *>(b);
+        d.ws.rows = reinterpret_cast<int32_t *>(b + kNoAllocRowsOff);
+        d.ws.slots = reinterpret_cast<uint2 *>(b + kNoAllocSlotsOff);
+        d.ws.rows_cap = kNoAllocMaxRows;
+        d.ws.vocab_cap = kNoAllocMaxVocab;
+        d.ws.nslots = kNoAllocSlots;
+        d.ready = true;
+    }
+    *out = &d.ws;
+    return NOEL_OK;
+}
+
+}  // namespace
+
+extern "C" int noel_sampler_sample_batch_noalloc(const noel_sampler_config_t *cfg, const void *d_logits,
+                                                 int dtype, int batch, int vocab, size_t ld,
+                                                 const int32_t *d_history, int history_len, size_t hld,
+                                                 uint64_t *d_rng, int32_t *d_ids, float *d_probs, void *stream) {
+    if (batch > kNoAllocMaxRows || vocab > kNoAllocMaxVocab)
+        return fail(NOEL_ERR_TOO_LARGE,
+                    "noalloc entry point handles at most %d rows of at most %d tokens (got %d x %d); "
+                    "use noel_sampler_sample_batch",
+                    kNoAllocMaxRows, kNoAllocMaxVocab, batch, vocab);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(NOEL_ERR_NO_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return fail(NOEL_ERR_NO_DEVICE, "device ordinal %d", dev);
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    const Workspace *ws = nullptr;
+    r = noalloc_setup(dev, c, &ws);
+    if (r) return r;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    /* the array keeps the last call's contents: the row list starts empty */
+    CUDA_TRY(cudaMemsetAsync(ws->counters, 0, 4 * sizeof(int32_t), s));
+    noel_sample_extras_t ex{};
+    ex.d_probs = d_probs;
+    return sample_batch(cfg, d_logits, dtype, batch, vocab, ld, d_history, history_len, hld, d_rng, d_ids, &ex,
+                        s, ws);
 }
