@@ -264,12 +264,28 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         hist_bytes = W * 4 + (G + 1) * 4 + (size_t)(H - a.hist_start > 1 ? H - a.hist_start : 1) * 4;
         hist_bytes = (hist_bytes + 15) & ~size_t(15);
     }
-    size_t smem_main = hist_bytes;
+    size_t smem_main;
     if (block_kernel) {
-        smem_main += (size_t)a.cap * 8 + kWarmBins * 4;
-    } else if (mode != kGreedy) {
-        const int nw = kRowWarps;
-        smem_main += (size_t)nw * a.cap * 8 + (size_t)nw * 256 * 4 + (size_t)kUnionCap * 16;
+        smem_main = hist_bytes + (size_t)a.cap * 8 + kWarmBins * 4;
+    } else {
+        /* single-pass kernel: Bloom filter + (id, count) table of the window,
+         * per-warp buffers, and one area reused by the warm-up histogram and
+         * the row-end gather (keys, ids, then the sort keys) */
+        smem_main = 0;
+        if (a.penalty) {
+            const int win = H - a.hist_start > 1 ? H - a.hist_start : 1;
+            a.hcap = pow2_at_least(2 * win > 64 ? 2 * win : 64);
+            smem_main += (size_t)kBloomWords * 4 + (size_t)a.hcap * 8;
+        }
+        if (mode != kGreedy) {
+            const int nw = kRowWarps;
+            const int kw = a.kprime / 2 > 8 ? a.kprime / 2 : 8;
+            a.ucap = mode == kTopK ? nw * 2 * kw : nw * a.cap;
+            const size_t gather = (size_t)a.ucap * 8 + (size_t)pow2_at_least(a.ucap) * 8;
+            const size_t warm = mode == kTopK ? (size_t)2 * kWarpBins * 4 : 0;
+            smem_main += (size_t)nw * kQueueCap * (sizeof(V8) + 4) + (size_t)nw * a.cap * 8 +
+                         (gather > warm ? gather : warm);
+        }
     }
     const size_t smem_exact = a.penalty && !a.wb ? hist_bytes : 0;
     if (smem_main > c->smem_optin - 2048 || smem_exact > c->smem_optin - 16384)

@@ -69,6 +69,8 @@ struct SampleArgs {
     int top_k;
     int kprime;                 // kept-set size for top-k
     int cap;                    // candidate buffer entries
+    int hcap;                   // history hash-table slots (single-pass kernel)
+    int ucap;                   // gathered-candidate entries (single-pass kernel)
     uint64_t *rng;
     int32_t *ids;
     float *probs;

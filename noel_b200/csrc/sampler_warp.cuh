@@ -1,23 +1,30 @@
 /*
  * The single-pass sampling kernel for greedy rows, top-k rows with k <= 120
- * and full-list rows (top-k off): one CTA per row, eight warps that stream
- * their own slices of the row without block barriers.
+ * and full-list rows (top-k off): one small CTA (4 warps) per row, warps that
+ * stream their own slices of the row without block barriers, and a shared-
+ * memory footprint small enough for eight CTAs per SM, so the per-row phases
+ * of one CTA (history set-up, warm-up, finish) overlap the streaming of others.
  *
- * Row start: the CTA builds the history bitmap and per-id counts in shared
- * memory (sampler.c:87-103).  Streaming: warp w reads its eighth of the row
- * with 256-bit loads (four in flight per lane), applies the penalty, takes
- * the maximum of each 8-element vector and only looks at single elements
- * when that maximum can pass the current threshold:
- *   top-k  - the best (logit desc, id asc) key that K' kept elements beat;
- *            every warp keeps its own buffer, compacts it by a warp radix
- *            select when it fills, and publishes its threshold to the other
- *            warps (a shared 64-bit atomicMax), which filter with it too;
- *   full   - the -15 cut under the row's running max, shared the same way;
- *   greedy - the running (value, lowest id) maximum.
- * Row end: the warps' candidates are gathered and warp 0 alone computes the
- * weights, sorts them and runs the sequential mass / nucleus / draw loops
- * (sampler.c:119-191) while the CTA's other warps retire, so other CTAs on
- * the SM keep the memory system busy.
+ * Row start: the window of the row's history becomes a Bloom filter and an
+ * open-addressing table of (id, occurrences) (sampler.c:87-93).
+ * Streaming: warp w reads its quarter of the row with 256-bit
+ * ld.global.nc.L1::no_allocate.L2::evict_first loads (one batch prefetched),
+ * takes the maximum of each vector and only looks at single elements when
+ * that raw maximum can pass the current threshold.  The repetition penalty
+ * only lowers values (sampler.c:96-100), so it is applied exactly, but only to
+ * vectors that can pass.  Thresholds:
+ *   top-k  - the K' = pow2(k+8) best (logit desc, id asc).  A block warm-up on
+ *            the first batches starts near the K'-th largest; each warp keeps
+ *            its own best K'/2 in a shared-memory buffer, compacts it with a
+ *            register bitonic sort when it fills and publishes a ladder of its
+ *            kept keys; any combination with K' retained keys above it is a
+ *            valid filter for every warp.
+ *   full   - the -15 cut under the running maximum (sampler.c:137-138).
+ *   greedy - the running (value desc, id asc) maximum (sampler.c:106-116).
+ * Row end: warp 0 gathers the kept keys, selects the K' best, checks that no
+ * excluded element could belong to the top k (else the row goes to the
+ * two-pass kernel), computes the weights and runs the sequential mass /
+ * nucleus / draw loops of sampler.c:160-191.
  */
 #pragma once
 
@@ -25,18 +32,96 @@
 
 namespace noel {
 
-constexpr int kUnionCap = 1024;  // row-end gather / sort area (entries)
-constexpr int kRowWarps = 4;     // warps streaming one row
+constexpr int kRowWarps = 4;  // warps streaming one row
 constexpr int kRowThreads = 32 * kRowWarps;
+constexpr int kWarpBins = 512;    // per level of the warm-up histogram (9 key bits)
+constexpr int kBloomWords = 512;  // 16384-bit Bloom filter of the history ids
 
-/* Bin of the K-th largest count in a 2048-bin histogram (counted from the top
- * bin down), found by all NT threads: each owns 2048/NT consecutive bins.
- * Returns the bin (or -1 if the total is below K); *need_in_bin = how many of
- * that bin's entries are needed. */
+/* ---------------------------------------------------------------------- */
+/* the row's history: Bloom filter + open-addressing (id -> occurrences)    */
+
+struct HistSet {
+    uint32_t *bloom;  // kBloomWords
+    uint32_t *key;    // cap: id + 1, 0 = empty
+    uint32_t *cnt;    // cap: occurrences in the window
+    int cap;          // power of two >= 2 x window
+};
+
+__device__ __forceinline__ uint32_t hs_hash(uint32_t id) {
+    return id * 0x9E3779B1u;  // Fibonacci hashing
+}
+
+template <int NT>
+__device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H, int V) {
+    for (int i = threadIdx.x; i < kBloomWords; i += NT) h.bloom[i] = 0u;
+    for (int i = threadIdx.x; i < h.cap; i += NT) {
+        h.key[i] = 0u;
+        h.cnt[i] = 0u;
+    }
+    __syncthreads();
+    const int bits = __ffs(h.cap) - 1;
+    for (int i = first + threadIdx.x; i < H; i += NT) {
+        const int t = hrow[i];
+        if (t < 0 || t >= V) continue;  // sampler.c:95
+        const uint32_t hh = hs_hash((uint32_t)t);
+        const uint32_t b = hh >> 18;  // 14 bits
+        atomicOr(&h.bloom[b >> 5], 1u << (b & 31));
+        uint32_t p = bits ? (hh >> (32 - bits)) : 0u;
+        for (int probe = 0; probe < h.cap; ++probe) {
+            const uint32_t prev = atomicCAS(&h.key[p], 0u, (uint32_t)t + 1u);
+            if (prev == 0u || prev == (uint32_t)t + 1u) {
+                atomicAdd(&h.cnt[p], 1u);
+                break;
+            }
+            p = (p + 1) & (uint32_t)(h.cap - 1);
+        }
+    }
+    __syncthreads();
+}
+
+/* occurrences of id in the window (0 if none) */
+__device__ __forceinline__ uint32_t hs_count(const HistSet &h, uint32_t id) {
+    const uint32_t hh = hs_hash(id);
+    const uint32_t b = hh >> 18;
+    if (!((h.bloom[b >> 5] >> (b & 31)) & 1u)) return 0u;
+    const int bits = __ffs(h.cap) - 1;
+    uint32_t p = bits ? (hh >> (32 - bits)) : 0u;
+    for (int probe = 0; probe < h.cap; ++probe) {
+        const uint32_t k = h.key[p];
+        if (k == id + 1u) return h.cnt[p];
+        if (k == 0u) return 0u;
+        p = (p + 1) & (uint32_t)(h.cap - 1);
+    }
+    return 0u;
+}
+
+/* the penalty on N consecutive ids starting at id0 (sampler.c:93-102) */
+template <int N>
+__device__ __forceinline__ void hs_penalize(const HistSet &h, uint32_t id0, float *x, float rep) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        const uint32_t c = hs_count(h, id0 + j);
+        if (c) x[j] = apply_penalty(x[j], c, rep);
+    }
+}
+
+/* penalised values written back to the caller's fp32 row, once per distinct id */
+template <int NT>
+__device__ void hs_write_back(const SampleArgs &a, const HistSet &h, int row) {
+    float *wrow = a.wb + (size_t)row * a.ld;
+    for (int s = threadIdx.x; s < h.cap; s += NT) {
+        const uint32_t k = h.key[s];
+        if (k) wrow[k - 1] = apply_penalty(wrow[k - 1], h.cnt[s], a.rep);
+    }
+}
+
+/* Bin of the K-th largest count of a kWarpBins histogram (counted from the top
+ * bin down), found by all NT threads; -1 if the total is below K.
+ * *need_in_bin = how many of that bin's entries are needed. */
 template <int NT>
 __device__ int block_find_bin_desc(const uint32_t *h, int K, int *s_w, int *s_res, int *need_in_bin) {
-    constexpr int PER = 2048 / NT;
-    const int hi = 2047 - threadIdx.x * PER;  // this thread's bins: hi, hi-1, ..., hi-PER+1
+    constexpr int PER = kWarpBins / NT;
+    const int hi = kWarpBins - 1 - threadIdx.x * PER;
     int c[PER], sum = 0;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
@@ -63,410 +148,387 @@ __device__ int block_find_bin_desc(const uint32_t *h, int K, int *s_w, int *s_re
     return s_res[0];
 }
 
-template <typename T, int MODE>
-__global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kernel(const SampleArgs a) {
-    using F = Fmt<T>;
-    constexpr int NT = kRowThreads, NW = NT / 32;
-    constexpr int VEC = F::VEC, U = F::U, NE = U * VEC;
-    static_assert(NE <= 32, "pending mask is 32 bits");
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ unsigned long long s_taus[NW];  // each warp's own exclusion threshold
-    __shared__ unsigned long long s_btau;      // block warm-up threshold (top-k)
-    __shared__ unsigned long long s_tsh;       // best shared filter (warm-up or ladders)
-    __shared__ unsigned long long s_lad[3][NW];  // each warp's (2kw/NW)-th, (kw/2)-th, kw-th kept key
-    __shared__ int s_res[2];
-    __shared__ uint32_t s_maxkey;
-    __shared__ int s_flags, s_l0nan, s_trunc;
-    __shared__ int s_wcnt[NW];
-    __shared__ int s_wfill[NW];  // entries each warp has claimed in its buffer
-    __shared__ int s_w[NW + 1];
-    __shared__ float s_gx[NW];
-    __shared__ uint32_t s_gid[NW];
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int row = blockIdx.x;
-    const int V = a.vocab;
-    const void *rowp = static_cast<const char *>(a.logits) + (size_t)row * (size_t)a.ld * F::ES;
+/* 16 elements per lane per batch: two 8-float vectors or one 16-bf16 vector */
+template <typename T>
+struct WarpFmt;
+template <>
+struct WarpFmt<float> {
+    static constexpr int VEC = 8, U = 2;
+};
+template <>
+struct WarpFmt<uint16_t> {
+    static constexpr int VEC = 16, U = 1;
+};
+constexpr int kLaneElems = 16;
+constexpr int kQueueCap = 64;  // queued vectors per warp (>= the vectors of one batch)
 
-    /* ---- shared-memory carve-up ---- */
-    unsigned char *sp = smem;
-    HistView hv{nullptr, nullptr, nullptr, 0};
-    if (a.penalty) {
-        hv.words = (V + 31) >> 5;
-        const int G = (hv.words + 7) >> 3;
-        hv.bm = reinterpret_cast<uint32_t *>(sp);
-        sp += (size_t)hv.words * 4;
-        hv.gpre = reinterpret_cast<uint32_t *>(sp);
-        sp += (size_t)(G + 1) * 4;
-        hv.cnt = reinterpret_cast<uint32_t *>(sp);
-        sp += (size_t)max(1, a.hist_len - a.hist_start) * 4;
-        sp = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(sp) + 15) & ~uintptr_t(15));
-    }
-    const int capw = a.cap;  // per-warp buffer entries
-    uint32_t *wkey = nullptr, *wid = nullptr, *whist = nullptr;
-    uint32_t *ukey = nullptr, *uid = nullptr;
-    uint64_t *sk = nullptr;
+/* one lane's batch, passed by value to the out-of-line paths */
+struct LaneBatch {
+    float v[kLaneElems];
+};
+
+/* a 32-byte vector to / from shared memory as two 16-byte accesses */
+__device__ __forceinline__ void st_vec(V8 *dst, const V8 &v) {
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    d[0] = make_uint4(v.v[0], v.v[1], v.v[2], v.v[3]);
+    d[1] = make_uint4(v.v[4], v.v[5], v.v[6], v.v[7]);
+}
+__device__ __forceinline__ V8 ld_vec(const V8 *src) {
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    const uint4 a = s[0], b = s[1];
+    V8 v;
+    v.v[0] = a.x, v.v[1] = a.y, v.v[2] = a.z, v.v[3] = a.w;
+    v.v[4] = b.x, v.v[5] = b.y, v.v[6] = b.z, v.v[7] = b.w;
+    return v;
+}
+
+/* ---------------------------------------------------------------------- */
+/* the row's shared state                                                   */
+
+struct RowShared {
+    unsigned long long tsh;                 // best shared top-k filter
+    unsigned long long taus[kRowWarps];     // each warp's own exclusion threshold
+    unsigned long long lad[3][kRowWarps];   // each warp's (2kw/NW)-th, (kw/2)-th, kw-th kept key
+    int res[2];
+    uint32_t maxkey;                        // running maximum key (full list)
+    int flags, l0nan, trunc;
+    int wcnt[kRowWarps];
+    int wfill[kRowWarps];
+    int w[kRowWarps + 1];
+    float gx[kRowWarps];
+    uint32_t gid[kRowWarps];
+};
+__shared__ RowShared rs;
+extern __shared__ __align__(32) unsigned char row_smem[];
+
+/* Dynamic shared memory of one row, recomputed from the arguments wherever it
+ * is needed: vector queues, the history set, per-warp candidate buffers and
+ * one area reused by the warm-up histogram and the row-end gather. */
+struct RowLayout {
+    V8 *q;              // this warp's queue
+    uint32_t *qid;      // id of each queued vector's first element
+    HistSet hs;
+    uint32_t *wkey, *wid;  // this warp's candidate buffer
+    uint32_t *area, *ukey, *uid;
+    uint64_t *sk;
+};
+
+template <int MODE>
+__device__ __forceinline__ RowLayout row_layout(const SampleArgs &a, int warp) {
+    constexpr int NW = kRowWarps;
+    unsigned char *sp = row_smem;
+    RowLayout L;
+    L.q = nullptr;
+    L.qid = nullptr;
     if (MODE != kGreedy) {
-        uint32_t *wb = reinterpret_cast<uint32_t *>(sp);
-        wkey = wb + (size_t)warp * capw * 2;
-        wid = wkey + capw;
-        sp += (size_t)NW * capw * 8;
-        whist = reinterpret_cast<uint32_t *>(sp) + warp * 256;
-        sp += (size_t)NW * 256 * 4;
-        ukey = reinterpret_cast<uint32_t *>(sp);
-        uid = ukey + kUnionCap;
-        sp += (size_t)kUnionCap * 8;
-        sk = reinterpret_cast<uint64_t *>(sp);
+        L.q = reinterpret_cast<V8 *>(sp) + warp * kQueueCap;
+        sp += NW * kQueueCap * sizeof(V8);
+        L.qid = reinterpret_cast<uint32_t *>(sp) + warp * kQueueCap;
+        sp += NW * kQueueCap * 4;
     }
-
-    if (tid < NW) {
-        s_wfill[tid] = 0;
-        s_taus[tid] = 0ull;
-        s_lad[0][tid] = s_lad[1][tid] = s_lad[2][tid] = 0ull;
+    L.hs = HistSet{nullptr, nullptr, nullptr, 0};
+    if (a.penalty) {
+        L.hs.bloom = reinterpret_cast<uint32_t *>(sp);
+        sp += kBloomWords * 4;
+        L.hs.cap = a.hcap;
+        L.hs.key = reinterpret_cast<uint32_t *>(sp);
+        sp += a.hcap * 4;
+        L.hs.cnt = reinterpret_cast<uint32_t *>(sp);
+        sp += a.hcap * 4;
     }
-    if (MODE == kTopK)
-        for (int i = tid; i < 2048; i += NT) ukey[i] = 0u;  // warm-up bins (the gather area)
-    if (tid == 0) {
-        s_btau = 0ull;
-        s_tsh = 0ull;
-        s_maxkey = kKeyNegInf;
-        s_flags = 0;
-        s_l0nan = 0;
-        s_trunc = 0;
+    L.wkey = L.wid = L.area = L.ukey = L.uid = nullptr;
+    L.sk = nullptr;
+    if (MODE != kGreedy) {
+        L.wkey = reinterpret_cast<uint32_t *>(sp) + warp * a.cap * 2;
+        L.wid = L.wkey + a.cap;
+        sp += NW * a.cap * 8;
+        /* warm-up bins (2 x kWarpBins), later the gather (ucap keys and ids)
+         * followed by the sort keys (pow2(ucap) x u64) */
+        L.area = reinterpret_cast<uint32_t *>(sp);
+        L.ukey = L.area;
+        L.uid = L.area + a.ucap;
+        L.sk = reinterpret_cast<uint64_t *>(L.area + 2 * a.ucap);
     }
-    if (a.penalty) build_history<NT>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w);
-    __syncthreads();
+    return L;
+}
 
-    const RowGeom g = row_geom<T>(rowp, V);
-    const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
-    const int per = (g.nvec + NW - 1) / NW;
-    const int v0 = min(g.nvec, warp * per), v1 = min(g.nvec, v0 + per);
+__device__ __forceinline__ int warp_kw(const SampleArgs &a) { return max(8, a.kprime / 2); }
 
-    const int kw = max(8, a.kprime / 2);  // entries a warp keeps (top-k mode)
-    int wcount = 0;
-    bool wtrunc = false;
-    unsigned long long tau_w = 0ull;
-    float gx = -INFINITY;
-    uint32_t gid = 0xFFFFFFFFu;
-    bool stop = false;
+/* ---------------------------------------------------------------------- */
+/* out-of-line paths                                                        */
 
-    /* ---- scalar head / tail (warp 0) ---- */
-    if (warp == 0) {
-        const bool have = lane < g.nscalar;
-        float xs = 0.0f;
-        int ids = 0;
-        if (have) {
-            ids = scalar_id(g, lane);
-            xs = F::scalar(rowp, ids);
-            if (a.penalty && ((hv.bm[ids >> 5] >> (ids & 31)) & 1u))
-                xs = apply_penalty(xs, hv.cnt[hist_rank(hv, ids)], a.rep);
-            if (ids == 0 && xs != xs) s_l0nan = 1;
+/* Lane-local insertion of the pend elements of x (ids id0 + e) into the
+ * warp's buffer; clears pend for the elements that found a slot. */
+template <int N>
+__device__ __forceinline__ void buffer_insert(const RowLayout &L, int warp, int capw, const float (&x)[N],
+                                              uint32_t id0, uint32_t &pend) {
+    int slot = atomicAdd(&rs.wfill[warp], __popc(pend));
+    uint32_t pp = pend;
+    while (pp) {
+        const int e = __ffs(pp) - 1;
+        pp &= pp - 1;
+        if (slot < capw) {
+            float xv = x[0];
+#pragma unroll
+            for (int q = 1; q < N; ++q) xv = (q == e) ? x[q] : xv;
+            L.wkey[slot] = ord_key(xv);
+            L.wid[slot] = id0 + (uint32_t)e;
+            pend &= ~(1u << e);
         }
-        if (MODE == kGreedy) {
-            if (have && (xs > gx || (xs == gx && (uint32_t)ids < gid))) {
-                gx = xs;
-                gid = (uint32_t)ids;
+        ++slot;
+    }
+}
+
+/* Keep the warp's best kw entries, publish its threshold and ladder, and raise
+ * the row's shared filter to the best combination the ladders prove. */
+__device__ __forceinline__ unsigned long long warp_compact(const RowLayout &L, int warp, int capw, int kw) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+    const int n = min(*(volatile int *)&rs.wfill[warp], capw);
+    __syncwarp();
+    uint64_t lad[3];
+    const unsigned long long tau_w = warp_topk_sorted_r<4>(L.wkey, L.wid, n, kw, lad, max(1, 2 * kw / kRowWarps));
+    if (lane == 0) {
+        rs.wfill[warp] = kw;
+        rs.taus[warp] = tau_w;
+        rs.lad[0][warp] = lad[0];
+        rs.lad[1][warp] = lad[1];
+        rs.lad[2][warp] = lad[2];
+        __threadfence_block();
+        /* K' retained elements beat each of: every warp's (2kw/NW)-th, the 4th
+         * largest (kw/2)-th, the 2nd largest kw-th */
+        unsigned long long mn = ~0ull, q4[4] = {0ull, 0ull, 0ull, 0ull}, c1 = 0ull, c2 = 0ull;
+        for (int w = 0; w < kRowWarps; ++w) {
+            const unsigned long long l0 = *(volatile unsigned long long *)&rs.lad[0][w];
+            const unsigned long long l1 = *(volatile unsigned long long *)&rs.lad[1][w];
+            const unsigned long long l2 = *(volatile unsigned long long *)&rs.lad[2][w];
+            mn = min(mn, l0);
+            for (int q = 0; q < 4; ++q)
+                if (l1 > q4[q]) {
+                    for (int z = 3; z > q; --z) q4[z] = q4[z - 1];
+                    q4[q] = l1;
+                    break;
+                }
+            if (l2 > c1) {
+                c2 = c1;
+                c1 = l2;
+            } else if (l2 > c2) {
+                c2 = l2;
             }
-        } else {
-            const bool ins = have && xs == xs;
-            const uint32_t b = __ballot_sync(kFull, ins);
-            if (ins) {
-                const int pos = __popc(b & lanemask_lt());
-                wkey[pos] = ord_key(xs);
-                wid[pos] = (uint32_t)ids;
-            }
-            wcount = __popc(b);
-            if (lane == 0) s_wfill[0] = wcount;
-            if (MODE == kFullList) {
-                const float m = warp_max_f(ins ? xs : -INFINITY);
-                if (lane == 0 && m > -INFINITY) atomicMax(&s_maxkey, ord_key(m));
-            }
+        }
+        if (kRowWarps < 4) q4[3] = 0ull;
+        atomicMax(&rs.tsh, max(max(mn, q4[3]), c2));
+    }
+    __syncwarp();
+    return tau_w;
+}
+
+/* Top-k drain of the warp's n queued vectors, one per lane per round: the
+ * penalty, the exact (logit desc, id asc) test against the current filter,
+ * insertion, and compaction whenever the buffer fills.  Returns the warp's
+ * own threshold. */
+template <typename T>
+__device__ __noinline__ unsigned long long topk_drain(const SampleArgs &a, int n, unsigned long long tau_w) {
+    constexpr int VEC = Fmt<T>::VEC;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const RowLayout L = row_layout<kTopK>(a, warp);
+    const int capw = a.cap, kw = warp_kw(a);
+    for (int r = 0; r < n; r += 32) {
+        const int i = r + lane;
+        float x[VEC];
+        uint32_t id0 = 0u, pend = 0u;
+        if (i < n) {
+            Fmt<T>::unpack(ld_vec(L.q + i), x);
+            id0 = L.qid[i];
+            if (a.penalty) hs_penalize<VEC>(L.hs, id0, x, a.rep);
+            const unsigned long long te = max(tau_w, *(volatile unsigned long long *)&rs.tsh);
+            const uint32_t tk = (uint32_t)(te >> 32);
+            const float tau_f = tk == 0u ? -INFINITY : key_float(tk);
+            const uint32_t tau_id = 0xFFFFFFFFu - (uint32_t)te;  // ties at tau_f pass below this id
+#pragma unroll
+            for (int j = 0; j < VEC; ++j)
+                if (x[j] > tau_f || (x[j] == tau_f && id0 + j < tau_id)) pend |= 1u << j;
+        }
+        for (;;) {
+            if (!__any_sync(kFull, pend != 0u)) break;
+            if (pend) buffer_insert<VEC>(L, warp, capw, x, id0, pend);
+            if (!__any_sync(kFull, pend != 0u)) break;
+            tau_w = warp_compact(L, warp, capw, kw);  // the buffer is full
+            const unsigned long long te = max(tau_w, *(volatile unsigned long long *)&rs.tsh);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j)
+                if (((pend >> j) & 1u) && !(comp_key(ord_key(x[j]), id0 + j) > te)) pend &= ~(1u << j);
+        }
+    }
+    return tau_w;
+}
+
+/* Full-list drain (top-k off): penalises the queued vectors, raises the
+ * running maximum, inserts what passes the -15 cut under it and drops what
+ * the new maximum cuts when the buffer fills.  Sets kOverflow when the kept
+ * list outgrows the buffer. */
+template <typename T>
+__device__ __noinline__ void full_drain(const SampleArgs &a, int n) {
+    constexpr int VEC = Fmt<T>::VEC;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const RowLayout L = row_layout<kFullList>(a, warp);
+    const int capw = a.cap;
+    for (int r = 0; r < n; r += 32) {
+        const int i = r + lane;
+        float x[VEC];
+        uint32_t id0 = 0u, pend = 0u;
+        float lm = -INFINITY;
+        if (i < n) {
+            Fmt<T>::unpack(ld_vec(L.q + i), x);
+            id0 = L.qid[i];
+            if (a.penalty) hs_penalize<VEC>(L.hs, id0, x, a.rep);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) lm = fmaxf(lm, x[j]);
+        }
+        lm = warp_max_f(lm);
+        if (lane == 0 && lm > -INFINITY) atomicMax(&rs.maxkey, ord_key(lm));
+        __syncwarp();
+        float m = key_float(*(volatile uint32_t *)&rs.maxkey);
+        if (i < n) {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j)
+                if (scaled_diff(x[j], m, a.inv_t) > -15.0f) pend |= 1u << j;
+        }
+        for (;;) {
+            if (!__any_sync(kFull, pend != 0u)) break;
+            if (pend) buffer_insert<VEC>(L, warp, capw, x, id0, pend);
+            if (!__any_sync(kFull, pend != 0u)) break;
             __syncwarp();
+            int nb = min(*(volatile int *)&rs.wfill[warp], capw);
+            __syncwarp();
+            m = key_float(*(volatile uint32_t *)&rs.maxkey);
+            nb = warp_filter_by_max(L.wkey, L.wid, nb, m, a.inv_t);
+            if (lane == 0) rs.wfill[warp] = nb;
+            __syncwarp();
+            if (nb > capw / 2) {
+                if (lane == 0) atomicOr(&rs.flags, kOverflow);
+                return;
+            }
+#pragma unroll
+            for (int j = 0; j < VEC; ++j)
+                if (((pend >> j) & 1u) && !(scaled_diff(x[j], m, a.inv_t) > -15.0f)) pend &= ~(1u << j);
         }
     }
+}
 
-    /* ---- the warp's slice of the vector body, next batch prefetched ---- */
-    V8 nxt[U];
+/* Greedy slow path for one lane (repetition penalty on): penalises the
+ * candidate vectors and folds them into the lane's (value desc, id asc) best. */
+template <int VEC, int U>
+__device__ __noinline__ uint64_t greedy_take(const SampleArgs &a, uint32_t id0, uint32_t cand, float gx,
+                                             uint32_t gid, LaneBatch b) {
+    const RowLayout L = row_layout<kGreedy>(a, threadIdx.x >> 5);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        if (!((cand >> u) & 1u)) continue;
+        const uint32_t v0 = id0 + (uint32_t)(u * 32 * VEC);
+        float x[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) x[j] = b.v[u * VEC + j];
+        hs_penalize<VEC>(L.hs, v0, x, a.rep);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+            if (x[j] > gx || (x[j] == gx && v0 + j < gid)) {
+                gx = x[j];
+                gid = v0 + j;
+            }
+    }
+    return ((uint64_t)__float_as_uint(gx) << 32) | gid;
+}
+
+/* Block warm-up on every warp's first batch (all threads of the block): the
+ * smallest lane maximum of a warp has 32 of the warp's elements above it; the
+ * second largest of those bounds a two-level histogram (9 key bits, then the
+ * next 9 inside the chosen bin) of the larger elements, whose bin holding the
+ * K'-th largest gives the row's starting threshold.  Returns the warp's own
+ * threshold. */
+template <typename T>
+__device__ __noinline__ unsigned long long row_warmup(const SampleArgs &a, int head, int v0, int v1) {
+    using F = Fmt<T>;
+    constexpr int NT = kRowThreads, NW = kRowWarps;
+    constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U, NE = U * VEC;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const RowLayout L = row_layout<kTopK>(a, warp);
+    float xw[NE];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
         const int vi = v0 + u * 32 + lane;
-        if (vi < v1) nxt[u] = ld_stream(vbase + vi);
+        if (vi < v1) {
+            F::unpack(ld_vec(L.q + u * 32 + lane), xw + u * VEC);
+            if (a.penalty) hs_penalize<VEC>(L.hs, (uint32_t)(head + vi * VEC), xw + u * VEC, a.rep);
+        } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) xw[u * VEC + j] = -INFINITY;
+        }
     }
-    if (MODE == kTopK && min(g.nvec, NW * 32 * U) * VEC >= 4 * a.kprime) {
-        /* Block warm-up on every warp's first batch: each warp's lane maxima
-         * give it a threshold with 32 elements above; the second largest of
-         * those bounds a histogram (2048 bins on the top 11 key bits) of the
-         * batch's larger elements, whose bin holding the K'-th largest gives
-         * the row's starting threshold. */
-        float xw[NE];
-        bool okw[U];
+    unsigned long long tau_w = 0ull;
+    float lmax = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int vi = v0 + u * 32 + lane;
-            okw[u] = vi < v1;
-            if (okw[u]) {
-                F::unpack(nxt[u], xw + u * VEC);
-                if (a.penalty) penalize_group<VEC>(hv, g.head + vi * VEC, xw + u * VEC, a.rep);
-            } else {
+    for (int e = 0; e < NE; ++e) lmax = fmaxf(lmax, xw[e]);  // NaN-ignoring
+    const float t0 = warp_min_f(lmax);
+    if (t0 > -INFINITY) {
+        tau_w = (unsigned long long)ord_key(t0) << 32;  // 32 of this warp's elements beat it
+        if (lane == 0) rs.taus[warp] = tau_w;
+    }
+    __syncthreads();
+    unsigned long long t1 = 0ull, t2 = 0ull;
 #pragma unroll
-                for (int j = 0; j < VEC; ++j) xw[u * VEC + j] = -INFINITY;
-            }
+    for (int w = 0; w < NW; ++w) {
+        const unsigned long long tw = rs.taus[w];
+        if (tw > t1) {
+            t2 = t1;
+            t1 = tw;
+        } else if (tw > t2) {
+            t2 = tw;
         }
-        float lmax = -INFINITY;
+    }
+    const uint32_t lo_key = (uint32_t)(t2 >> 32);
 #pragma unroll
-        for (int e = 0; e < NE; ++e) lmax = fmaxf(lmax, xw[e]);  // NaN-ignoring
-        const float t0 = warp_min_f(lmax);
-        if (t0 > -INFINITY) {
-            tau_w = (unsigned long long)ord_key(t0) << 32;  // 32 elements of this warp beat it
-            wtrunc = true;
-            if (lane == 0) s_taus[warp] = tau_w;
-        }
+    for (int e = 0; e < NE; ++e) {
+        const float xv = xw[e];
+        if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key) atomicAdd(&L.area[ord_key(xv) >> 23], 1u);
+    }
+    __syncthreads();
+    int need;
+    const int wb1 = block_find_bin_desc<NT>(L.area, a.kprime, rs.w, rs.res, &need);
+    if (wb1 >= 0) {
+        uint32_t *h2 = L.area + kWarpBins;
+        for (int i = tid; i < kWarpBins; i += NT) h2[i] = 0u;
         __syncthreads();
-        unsigned long long t1 = 0ull, t2 = 0ull;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const unsigned long long tw = s_taus[w];
-            if (tw > t1) { t2 = t1; t1 = tw; } else if (tw > t2) { t2 = tw; }
-        }
-        const uint32_t lo_key = (uint32_t)(t2 >> 32);
 #pragma unroll
         for (int e = 0; e < NE; ++e) {
             const float xv = xw[e];
-            if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key) atomicAdd(&ukey[ord_key(xv) >> 21], 1u);
+            if (xv == xv && xv > -INFINITY && (int)(ord_key(xv) >> 23) == wb1)
+                atomicAdd(&h2[(ord_key(xv) >> 14) & (kWarpBins - 1)], 1u);
         }
         __syncthreads();
-        /* level 1: bin (top 11 key bits) of the K'-th largest; level 2: the next
-         * 11 bits inside that bin */
-        int need;
-        const int wb = block_find_bin_desc<NT>(ukey, a.kprime, s_w, s_res, &need);
-        if (wb >= 0) {
-            uint32_t *h2 = ukey + 2048;  // second-level bins
-            for (int i = tid; i < 2048; i += NT) h2[i] = 0u;
-            __syncthreads();
-#pragma unroll
-            for (int e = 0; e < NE; ++e) {
-                const float xv = xw[e];
-                if (xv == xv && xv > -INFINITY && (int)(ord_key(xv) >> 21) == wb)
-                    atomicAdd(&h2[(ord_key(xv) >> 10) & 2047u], 1u);
-            }
-            __syncthreads();
-            int need2;
-            const int b2 = block_find_bin_desc<NT>(h2, need, s_w, s_res, &need2);
-            if (tid == 0 && b2 >= 0) {
-                const uint32_t key = ((uint32_t)wb << 21) | ((uint32_t)b2 << 10);
-                s_btau = (unsigned long long)key << 32;
-                s_tsh = s_btau;
-            }
-            __syncthreads();
+        int need2;
+        const int wb2 = block_find_bin_desc<NT>(h2, need, rs.w, rs.res, &need2);
+        if (tid == 0 && wb2 >= 0) {
+            const uint32_t key = ((uint32_t)wb1 << 23) | ((uint32_t)wb2 << 14);
+            rs.tsh = (unsigned long long)key << 32;  // K' first-batch elements beat it
         }
+        __syncthreads();
     }
+    return tau_w;
+}
 
-    for (int base = v0; base < v1; base += 32 * U) {
-        float x[NE];
-        float vm[U];
-        uint32_t valid = 0u;
-        {
-            V8 v[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) v[u] = nxt[u];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int vi = base + 32 * U + u * 32 + lane;
-                if (vi < v1) nxt[u] = ld_stream(vbase + vi);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int vi = base + u * 32 + lane;
-                if (vi < v1) {
-                    F::unpack(v[u], x + u * VEC);
-                    valid |= ((1u << VEC) - 1u) << (u * VEC);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < VEC; ++j) x[u * VEC + j] = -INFINITY;
-                }
-            }
-        }
-        if (base == 0 && lane == 0 && g.head == 0 && (valid & 1u) && x[0] != x[0]) s_l0nan = 1;
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            float m = x[u * VEC];
-#pragma unroll
-            for (int j = 1; j < VEC; ++j) m = fmaxf(m, x[u * VEC + j]);
-            vm[u] = m;  // NaN-free unless the whole vector is NaN
-        }
-
-        /* The penalty only lowers values (sampler.c:96-100), so a vector whose
-         * raw maximum cannot pass the filter needs no penalty lookup.  This
-         * applies it to vector u and returns the penalised maximum. */
-        uint32_t pdone = 0u;  // vectors already penalised in this batch
-        auto penalize_vec = [&](int u) -> float {
-            const int vi = base + u * 32 + lane;
-            if (!a.penalty || vi >= v1 || ((pdone >> u) & 1u)) return vm[u];
-            pdone |= 1u << u;
-            const int id0 = g.head + vi * VEC;
-            uint32_t bits = hist_bits(hv, id0, VEC);
-            if (!bits) return vm[u];
-            while (bits) {
-                const int j = __ffs(bits) - 1;
-                bits &= bits - 1;
-                const uint32_t c = hv.cnt[hist_rank(hv, id0 + j)];
-#pragma unroll
-                for (int jj = 0; jj < VEC; ++jj)
-                    if (jj == j) x[u * VEC + jj] = apply_penalty(x[u * VEC + jj], c, a.rep);
-            }
-            float m = x[u * VEC];
-#pragma unroll
-            for (int j = 1; j < VEC; ++j) m = fmaxf(m, x[u * VEC + j]);
-            vm[u] = m;
-            return m;
-        };
-
-        if (MODE == kGreedy) {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                if (vm[u] >= gx && penalize_vec(u) >= gx) {
-                    const uint32_t id0 = (uint32_t)(g.head + (base + u * 32 + lane) * VEC);
-#pragma unroll
-                    for (int j = 0; j < VEC; ++j) {
-                        const float xv = x[u * VEC + j];
-                        if (((valid >> (u * VEC + j)) & 1u) && (xv > gx || (xv == gx && id0 + j < gid))) {
-                            gx = xv;
-                            gid = id0 + j;
-                        }
-                    }
-                }
-            }
-            continue;
-        }
-
-        uint32_t pend = 0u;
-        float m_cur = 0.0f;
-        unsigned long long tau_eff = 0ull;
-        if (MODE == kTopK) {
-            tau_eff = max(tau_w, *(volatile unsigned long long *)&s_tsh);
-            const uint32_t tk = (uint32_t)(tau_eff >> 32);
-            const float tau_f = tk == 0u ? -INFINITY : key_float(tk);
-            const uint32_t tau_id = 0xFFFFFFFFu - (uint32_t)tau_eff;  // ties at tau_f pass below this id
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                if (vm[u] >= tau_f && penalize_vec(u) >= tau_f) {
-                    const uint32_t id0 = (uint32_t)(g.head + (base + u * 32 + lane) * VEC);
-#pragma unroll
-                    for (int j = 0; j < VEC; ++j) {
-                        const float xv = x[u * VEC + j];
-                        const bool pass = xv > tau_f || (xv == tau_f && id0 + j < tau_id);
-                        if (pass && ((valid >> (u * VEC + j)) & 1u)) pend |= 1u << (u * VEC + j);
-                    }
-                }
-            }
-        } else {
-            if (__any_sync(kFull, (*(volatile int *)&s_flags & kOverflow) != 0)) break;
-            /* the running max of penalised values: raw maxima are upper bounds,
-             * so only vectors whose raw max exceeds it are penalised first */
-            float lm = -INFINITY;
-            {
-                const float mk = key_float(*(volatile uint32_t *)&s_maxkey);
-#pragma unroll
-                for (int u = 0; u < U; ++u) lm = fmaxf(lm, vm[u] > mk ? penalize_vec(u) : vm[u]);
-            }
-            lm = warp_max_f(lm);
-            if (lane == 0 && lm > -INFINITY) atomicMax(&s_maxkey, ord_key(lm));
-            __syncwarp();
-            m_cur = key_float(*(volatile uint32_t *)&s_maxkey);
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                if (scaled_diff(vm[u], m_cur, a.inv_t) > -15.0f && scaled_diff(penalize_vec(u), m_cur, a.inv_t) > -15.0f) {
-#pragma unroll
-                    for (int j = 0; j < VEC; ++j)
-                        if (((valid >> (u * VEC + j)) & 1u) && scaled_diff(x[u * VEC + j], m_cur, a.inv_t) > -15.0f)
-                            pend |= 1u << (u * VEC + j);
-                }
-            }
-        }
-
-        /* ---- lane-local insert into the warp's buffer; compact when full ---- */
-        for (;;) {
-            if (!__any_sync(kFull, pend != 0u)) break;
-            if (pend) {
-                int slot = atomicAdd(&s_wfill[warp], __popc(pend));
-                uint32_t pp = pend;
-                while (pp) {  // compact loop: this path is rare
-                    const int e = __ffs(pp) - 1;
-                    pp &= pp - 1;
-                    if (slot < capw) {
-                        float xv = x[0];
-#pragma unroll
-                        for (int q = 1; q < NE; ++q) xv = (q == e) ? x[q] : xv;
-                        wkey[slot] = ord_key(xv);
-                        wid[slot] = (uint32_t)(g.head + (base + (e / VEC) * 32 + lane) * VEC + (e % VEC));
-                        pend &= ~(1u << e);
-                    }
-                    ++slot;
-                }
-            }
-            if (!__any_sync(kFull, pend != 0u)) break;
-            __syncwarp();
-            wcount = min(*(volatile int *)&s_wfill[warp], capw);
-            __syncwarp();
-            if (MODE == kTopK) {
-                uint64_t lad[3];
-                tau_w = warp_topk_sorted_r<4>(wkey, wid, wcount, kw, lad, max(1, 2 * kw / NW));
-                wcount = kw;
-                wtrunc = true;
-                if (lane == 0) {
-                    s_wfill[warp] = kw;
-                    s_taus[warp] = tau_w;
-                    s_lad[0][warp] = lad[0];
-                    s_lad[1][warp] = lad[1];
-                    s_lad[2][warp] = lad[2];
-                    __threadfence_block();
-                    /* K' retained elements beat each of: every warp's
-                     * (2kw/NW)-th, the 4th largest (kw/2)-th (NW >= 4), the
-                     * 2nd largest kw-th */
-                    unsigned long long mn = ~0ull, b[4] = {0ull, 0ull, 0ull, 0ull}, c1 = 0ull, c2 = 0ull;
-                    for (int w = 0; w < NW; ++w) {
-                        const unsigned long long l0 = *(volatile unsigned long long *)&s_lad[0][w];
-                        const unsigned long long l1 = *(volatile unsigned long long *)&s_lad[1][w];
-                        const unsigned long long l2 = *(volatile unsigned long long *)&s_lad[2][w];
-                        mn = min(mn, l0);
-                        for (int q = 0; q < 4; ++q)
-                            if (l1 > b[q]) {
-                                for (int z = 3; z > q; --z) b[z] = b[z - 1];
-                                b[q] = l1;
-                                break;
-                            }
-                        if (l2 > c1) { c2 = c1; c1 = l2; } else if (l2 > c2) { c2 = l2; }
-                    }
-                    if (NW < 4) b[3] = 0ull;
-                    atomicMax(&s_tsh, max(max(mn, b[3]), c2));
-                }
-                tau_eff = max(tau_w, *(volatile unsigned long long *)&s_tsh);
-                __syncwarp();
-#pragma unroll
-                for (int e = 0; e < NE; ++e)
-                    if ((pend >> e) & 1u) {
-                        const uint32_t id = (uint32_t)(g.head + (base + (e / VEC) * 32 + lane) * VEC + (e % VEC));
-                        if (!(comp_key(ord_key(x[e]), id) > tau_eff)) pend &= ~(1u << e);
-                    }
-            } else {
-                const float m = key_float(*(volatile uint32_t *)&s_maxkey);
-                wcount = warp_filter_by_max(wkey, wid, wcount, m, a.inv_t);
-                if (lane == 0) s_wfill[warp] = wcount;
-                __syncwarp();
-                if (wcount > capw / 2) {
-                    if (lane == 0) atomicOr(&s_flags, kOverflow);
-                    stop = true;
-                    break;
-                }
-#pragma unroll
-                for (int e = 0; e < NE; ++e)
-                    if (((pend >> e) & 1u) && !(scaled_diff(x[e], m, a.inv_t) > -15.0f)) pend &= ~(1u << e);
-            }
-        }
-        if (stop) break;
-    }
-
-    /* ====================== finish the row ====================== */
+/* Row end (all threads of the block): gather, exactness check, weights and
+ * the sequential tail of sampler.c:160-191. */
+template <typename T, int MODE>
+__device__ __noinline__ void row_finish(const SampleArgs &a, unsigned long long tau_w, float gx, uint32_t gid) {
+    constexpr int NT = kRowThreads, NW = kRowWarps;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row = blockIdx.x;
+    const RowLayout L = row_layout<MODE>(a, warp);
+    const int capw = a.cap, kw = warp_kw(a);
+    bool wtrunc = tau_w != 0ull;
+    int wcount = 0;
     if (MODE == kGreedy) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -478,21 +540,21 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
             }
         }
         if (lane == 0) {
-            s_gx[warp] = gx;
-            s_gid[warp] = gid;
+            rs.gx[warp] = gx;
+            rs.gid[warp] = gid;
         }
         __syncthreads();
-        if (a.wb && a.penalty) write_back_penalty<NT>(a, hv, row);
+        if (a.wb && a.penalty) hs_write_back<NT>(a, L.hs, row);
         if (tid == 0) {
-            float bx = s_gx[0];
-            uint32_t bid = s_gid[0];
+            float bx = rs.gx[0];
+            uint32_t bid = rs.gid[0];
             for (int w = 1; w < NW; ++w)
-                if (s_gx[w] > bx || (s_gx[w] == bx && s_gid[w] < bid)) {
-                    bx = s_gx[w];
-                    bid = s_gid[w];
+                if (rs.gx[w] > bx || (rs.gx[w] == bx && rs.gid[w] < bid)) {
+                    bx = rs.gx[w];
+                    bid = rs.gid[w];
                 }
             RowOut o;
-            o.id = (s_l0nan || bid == 0xFFFFFFFFu) ? 0 : (int)bid;  // sampler.c:106-116
+            o.id = (rs.l0nan || bid == 0xFFFFFFFFu) ? 0 : (int)bid;  // sampler.c:106-116
             o.prob = 1.0f;
             o.mass = 1.0f;
             o.n_topk = o.n_final = o.num_cands = 1;
@@ -507,30 +569,30 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
         return;
     }
 
-    if (MODE != kGreedy) wcount = min(*(volatile int *)&s_wfill[warp], capw);
-    __syncthreads();  // all warps done streaming: s_maxkey, s_flags final
-    if (a.wb && a.penalty) write_back_penalty<NT>(a, hv, row);
-    if (MODE == kFullList && (s_flags & kOverflow)) {
+    wcount = min(*(volatile int *)&rs.wfill[warp], capw);
+    __syncthreads();  // all warps done streaming: rs.maxkey, rs.flags final
+    if (a.wb && a.penalty) hs_write_back<NT>(a, L.hs, row);
+    if (MODE == kFullList && (rs.flags & kOverflow)) {
         if (tid == 0) list_exact_row(a, row);
         return;
     }
-    const float Mfull = s_l0nan ? __uint_as_float(0x7FC00000u) : key_float(s_maxkey);
+    const float Mfull = rs.l0nan ? __uint_as_float(0x7FC00000u) : key_float(rs.maxkey);
     if (MODE == kTopK) {
-        /* entries below the second largest threshold cannot make the top K' */
-        const unsigned long long t2 = s_tsh;
+        /* entries below the shared filter cannot make the top K' */
+        const unsigned long long t2 = rs.tsh;
         if (t2) {
             int wn = 0;
             for (int b0 = 0; b0 < wcount; b0 += 32) {
                 const int i = b0 + lane;
                 const bool ok = i < wcount;
-                const uint32_t k = ok ? wkey[i] : 0u, v = ok ? wid[i] : 0u;
+                const uint32_t k = ok ? L.wkey[i] : 0u, v = ok ? L.wid[i] : 0u;
                 const bool keep = ok && comp_key(k, v) >= t2;
                 const uint32_t bal = __ballot_sync(kFull, keep);
                 __syncwarp();
                 if (keep) {
                     const int pos = wn + __popc(bal & lanemask_lt());
-                    wkey[pos] = k;
-                    wid[pos] = v;
+                    L.wkey[pos] = k;
+                    L.wid[pos] = v;
                 }
                 wn += __popc(bal);
                 __syncwarp();
@@ -538,49 +600,49 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
             wcount = wn;
         }
         if (wcount > 2 * kw) {  // keeps the gather within its area
-            tau_w = warp_topk_sorted_r<4>(wkey, wid, wcount, kw, nullptr, 1);
+            tau_w = warp_topk_sorted_r<4>(L.wkey, L.wid, wcount, kw, nullptr, 1);
             wcount = kw;
             wtrunc = true;
         }
     } else {
-        wcount = warp_filter_by_max(wkey, wid, wcount, Mfull, a.inv_t);
+        wcount = warp_filter_by_max(L.wkey, L.wid, wcount, Mfull, a.inv_t);
     }
     if (lane == 0) {
-        s_wcnt[warp] = wcount;
-        s_taus[warp] = wtrunc ? tau_w : 0ull;  // final exclusion threshold of this warp
-        if (wtrunc) s_trunc = 1;
+        rs.wcnt[warp] = wcount;
+        rs.taus[warp] = wtrunc ? tau_w : 0ull;  // final exclusion threshold of this warp
+        if (wtrunc) rs.trunc = 1;
     }
     __syncthreads();
     int off = 0, nu = 0;
     for (int w = 0; w < NW; ++w) {
-        if (w < warp) off += s_wcnt[w];
-        nu += s_wcnt[w];
+        if (w < warp) off += rs.wcnt[w];
+        nu += rs.wcnt[w];
     }
-    if (nu > kUnionCap) {  // full list larger than the gather area: two-pass kernel
+    if (nu > a.ucap) {  // full list larger than the gather area: two-pass kernel
         if (tid == 0) list_exact_row(a, row);
         return;
     }
     for (int i = lane; i < wcount; i += 32) {
-        ukey[off + i] = wkey[i];
-        uid[off + i] = wid[i];
+        L.ukey[off + i] = L.wkey[i];
+        L.uid[off + i] = L.wid[i];
     }
     __syncthreads();
     if (warp != 0) return;
 
     /* ---- warp 0: the row's finish ---- */
     int n = nu;
-    bool trunc = s_trunc != 0 || s_tsh != 0ull;
+    bool trunc = rs.trunc != 0 || rs.tsh != 0ull;
     uint32_t t_last = 0u;
     if (MODE == kTopK && (n > a.kprime || trunc)) {
         /* Every excluded element must rank below the K'-th kept one: the
          * shared filter guarantees it; a warp's own cut does when the K'-th
          * kept key beats that warp's final threshold. */
         unsigned long long worst = 0ull;
-        for (int w = 0; w < NW; ++w) worst = max(worst, s_taus[w]);
+        for (int w = 0; w < NW; ++w) worst = max(worst, rs.taus[w]);
         const unsigned long long T =
             n < a.kprime ? 0ull
-                         : (a.kprime < 128 ? warp_topk_sorted_r<4>(ukey, uid, n, a.kprime, nullptr, 1)
-                                           : warp_topk_sorted_r<8>(ukey, uid, n, a.kprime, nullptr, 1));
+                         : (a.kprime < 128 ? warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1)
+                                           : warp_topk_sorted_r<8>(L.ukey, L.uid, n, a.kprime, nullptr, 1));
         if (n < a.kprime || !(T > worst)) {
             if (lane == 0) list_exact_row(a, row);
             return;
@@ -592,11 +654,11 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
     float M = Mfull;
     if (MODE == kTopK) {
         uint32_t mk = 0u;
-        if (trunc) mk = ukey[0];  // the kept entries are sorted: [0] is the row max
+        if (trunc) mk = L.ukey[0];  // the kept entries are sorted: [0] is the row max
         else
-            for (int i = lane; i < n; i += 32) mk = max(mk, ukey[i]);
+            for (int i = lane; i < n; i += 32) mk = max(mk, L.ukey[i]);
         mk = warp_max_u(mk);
-        M = (s_l0nan || n == 0) ? __uint_as_float(0x7FC00000u) : key_float(mk);
+        M = (rs.l0nan || n == 0) ? __uint_as_float(0x7FC00000u) : key_float(mk);
     }
     int P = 1;
     while (P < n) P <<= 1;
@@ -606,14 +668,13 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
         uint64_t kv = 0ull;
         bool cand = false;
         if (i < n) {
-            const int q = i;
-            const float d = scaled_diff(key_float(ukey[q]), M, a.inv_t);
+            const float d = scaled_diff(key_float(L.ukey[i]), M, a.inv_t);
             if (d > -15.0f) {
-                kv = ((uint64_t)__float_as_uint(ref_weight(d, a.et)) << 32) | (uint64_t)(0xFFFFFFFFu - uid[q]);
+                kv = ((uint64_t)__float_as_uint(ref_weight(d, a.et)) << 32) | (uint64_t)(0xFFFFFFFFu - L.uid[i]);
                 cand = true;
             }
         }
-        if (i < P) sk[i] = kv;
+        if (i < P) L.sk[i] = kv;
         ncand += __popc(__ballot_sync(kFull, cand));
     }
     __syncwarp();
@@ -626,13 +687,11 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
             bool bad = false;
             for (int b0 = 0; b0 + 1 < ncand; b0 += 32) {
                 const int i = b0 + lane;
-                bad |= (i + 1 < ncand) && ((uint32_t)(sk[i] >> 32) == (uint32_t)(sk[i + 1] >> 32));
+                bad |= (i + 1 < ncand) && ((uint32_t)(L.sk[i] >> 32) == (uint32_t)(L.sk[i + 1] >> 32));
             }
             sorted = !__any_sync(kFull, bad);
         }
-        if (!sorted) {
-            warp_bitonic_desc(sk, P);
-        }
+        if (!sorted) warp_bitonic_desc(L.sk, P);
     }
 
     bool more = false, exact = true;
@@ -640,7 +699,7 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
         more = true;  // every kept entry is a candidate: the row has more
         const float dl = scaled_diff(key_float(t_last), M, a.inv_t);
         const float v_last = dl > -15.0f ? ref_weight(dl, a.et) : 0.0f;
-        const float v_k = __uint_as_float((uint32_t)(sk[a.top_k - 1] >> 32));
+        const float v_k = __uint_as_float((uint32_t)(L.sk[a.top_k - 1] >> 32));
         exact = v_last < v_k;
     }
     if (!exact) {
@@ -652,12 +711,12 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
     float mass = 0.0f;
     if (lane == 0) {
         uint64_t st[2] = {a.rng[2 * (size_t)row], a.rng[2 * (size_t)row + 1]};
-        auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float((uint32_t)(sk[i] >> 32)); };
+        auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float((uint32_t)(L.sk[i] >> 32)); };
         const TailOut t = run_tail(fb ? 1 : ncand, more, a.top_k, a.top_p, st, w);
         a.rng[2 * (size_t)row] = st[0];
         a.rng[2 * (size_t)row + 1] = st[1];
         RowOut o;
-        o.id = fb ? 0 : (int)(0xFFFFFFFFu - (uint32_t)sk[t.pos]);
+        o.id = fb ? 0 : (int)(0xFFFFFFFFu - (uint32_t)L.sk[t.pos]);
         o.prob = __fdiv_rn(w(t.pos), t.mass);
         o.mass = t.mass;
         o.n_topk = t.n_topk;
@@ -679,8 +738,8 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
                     id = 0;
                     p = 1.0f;
                 } else {
-                    id = (int)(0xFFFFFFFFu - (uint32_t)sk[i]);
-                    p = __uint_as_float((uint32_t)(sk[i] >> 32));
+                    id = (int)(0xFFFFFFFFu - (uint32_t)L.sk[i]);
+                    p = __uint_as_float((uint32_t)(L.sk[i] >> 32));
                     if (!a.list_weights) p = __fdiv_rn(p, mass);
                 }
             }
@@ -688,6 +747,225 @@ __global__ void __launch_bounds__(kRowThreads, 16 / kRowWarps) sample_rows_kerne
             if (a.list_probs) a.list_probs[(size_t)row * a.list_len + i] = p;
         }
     }
+}
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __grid_constant__ SampleArgs a) {
+    using F = Fmt<T>;
+    constexpr int NT = kRowThreads, NW = kRowWarps;
+    constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U, NE = U * VEC;
+    static_assert(NE == kLaneElems, "sixteen elements per lane and batch");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int row = blockIdx.x;
+    const int V = a.vocab;
+    const void *rowp = static_cast<const char *>(a.logits) + (size_t)row * (size_t)a.ld * F::ES;
+
+    {
+        const RowLayout L = row_layout<MODE>(a, warp);
+        if (tid < NW) {
+            rs.wfill[tid] = 0;
+            rs.taus[tid] = 0ull;
+            rs.lad[0][tid] = rs.lad[1][tid] = rs.lad[2][tid] = 0ull;
+        }
+        if (MODE == kTopK)
+            for (int i = tid; i < kWarpBins; i += NT) L.area[i] = 0u;
+        if (tid == 0) {
+            rs.tsh = 0ull;
+            rs.maxkey = kKeyNegInf;
+            rs.flags = 0;
+            rs.trunc = 0;
+            const float x0 = F::scalar(rowp, 0);
+            rs.l0nan = x0 != x0;  // a NaN at id 0 (the penalty keeps it NaN)
+        }
+        if (a.penalty) hs_build<NT>(L.hs, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V);
+        __syncthreads();
+    }
+
+    const RowGeom g = row_geom<T>(rowp, V);
+    const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
+    const int per = (g.nvec + NW - 1) / NW;
+    const int v0 = min(g.nvec, warp * per), v1 = min(g.nvec, v0 + per);
+
+    float gx = -INFINITY;
+    uint32_t gid = 0xFFFFFFFFu;
+
+    /* ---- scalar head / tail (warp 0) ---- */
+    if (warp == 0) {
+        const RowLayout L = row_layout<MODE>(a, warp);
+        const bool have = lane < g.nscalar;
+        float xs = 0.0f;
+        int ids = 0;
+        if (have) {
+            ids = scalar_id(g, lane);
+            xs = F::scalar(rowp, ids);
+            if (a.penalty) {
+                const uint32_t c = hs_count(L.hs, (uint32_t)ids);
+                if (c) xs = apply_penalty(xs, c, a.rep);
+            }
+        }
+        if (MODE == kGreedy) {
+            if (have && (xs > gx || (xs == gx && (uint32_t)ids < gid))) {
+                gx = xs;
+                gid = (uint32_t)ids;
+            }
+        } else {
+            const bool ins = have && xs == xs;
+            const uint32_t b = __ballot_sync(kFull, ins);
+            if (ins) {
+                const int pos = __popc(b & lanemask_lt());
+                L.wkey[pos] = ord_key(xs);
+                L.wid[pos] = (uint32_t)ids;
+            }
+            if (lane == 0) rs.wfill[0] = __popc(b);
+            if (MODE == kFullList) {
+                const float m = warp_max_f(ins ? xs : -INFINITY);
+                if (lane == 0 && m > -INFINITY) atomicMax(&rs.maxkey, ord_key(m));
+            }
+            __syncwarp();
+        }
+    }
+
+    /* first batch of this warp's slice (greedy prefetch, top-k warm-up) */
+    V8 nxt[U];
+    if (MODE != kFullList) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int vi = v0 + u * 32 + lane;
+            if (vi < v1) nxt[u] = ld_stream(vbase + vi);
+        }
+    }
+
+    unsigned long long tau_w = 0ull;
+    if (MODE == kTopK && min(g.nvec, NW * 32 * U) * VEC >= 4 * a.kprime) {
+        /* the first batch goes through this warp's queue, still empty */
+        V8 *const q = reinterpret_cast<V8 *>(row_smem) + warp * kQueueCap;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (v0 + u * 32 + lane < v1) st_vec(q + u * 32 + lane, nxt[u]);
+        __syncwarp();
+        tau_w = row_warmup<T>(a, g.head, v0, v1);
+    }
+
+    /* ---- the warp's slice of the vector body ---- */
+    if (MODE == kGreedy) {
+        /* load (one batch prefetched), vector maxima, one comparison */
+        for (int base = v0; base < v1; base += 32 * U) {
+            V8 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) v[u] = nxt[u];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int vi = base + 32 * U + u * 32 + lane;
+                if (vi < v1) nxt[u] = ld_stream(vbase + vi);
+            }
+            const uint32_t id0 = (uint32_t)(g.head + (base + lane) * VEC);
+            uint32_t cand = 0u;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float x[VEC];
+                F::unpack(v[u], x);
+                float m = x[0];
+#pragma unroll
+                for (int j = 1; j < VEC; ++j) m = fmaxf(m, x[j]);
+                /* raw maximum: NaN only if the whole vector is NaN; the
+                 * penalty only lowers values */
+                if (base + u * 32 + lane < v1 && m >= gx) cand |= 1u << u;
+            }
+            if (cand) {
+                LaneBatch bt;
+#pragma unroll
+                for (int u = 0; u < U; ++u) F::unpack(v[u], bt.v + u * VEC);
+                if (a.penalty) {
+                    const uint64_t r = greedy_take<VEC, U>(a, id0, cand, gx, gid, bt);
+                    gx = __uint_as_float((uint32_t)(r >> 32));
+                    gid = (uint32_t)r;
+                } else {
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        if (!((cand >> u) & 1u)) continue;
+#pragma unroll
+                        for (int j = 0; j < VEC; ++j) {
+                            const float xv = bt.v[u * VEC + j];
+                            const uint32_t id = id0 + (uint32_t)(u * 32 * VEC + j);
+                            if (xv > gx || (xv == gx && id < gid)) {
+                                gx = xv;
+                                gid = id;
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    } else {
+        /* Top-k / full list: load, vector maxima, one comparison; vectors
+         * that pass are queued.  When the queue would overflow, the inner
+         * loop stops before that batch, the queue is drained out of line
+         * (one queued vector per lane) and streaming resumes at the same
+         * batch, so no call sits inside the streaming loop.  32 warps per SM
+         * keep enough loads in flight without a register prefetch. */
+        V8 *const wq = reinterpret_cast<V8 *>(row_smem) + warp * kQueueCap;
+        uint32_t *const wqid = reinterpret_cast<uint32_t *>(row_smem + NW * kQueueCap * sizeof(V8)) + warp * kQueueCap;
+        int qfill = 0;  // warp-uniform
+        int base = v0;
+        for (;;) {
+            for (; base < v1; base += 32 * U) {
+                V8 v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int vi = base + u * 32 + lane;
+                    if (vi < v1) v[u] = ld_stream(vbase + vi);
+                }
+                float bound;  // raw maxima below it cannot pass
+                if (MODE == kTopK) {
+                    const unsigned long long te = max(tau_w, *(volatile unsigned long long *)&rs.tsh);
+                    const uint32_t tk = (uint32_t)(te >> 32);
+                    bound = tk == 0u ? -INFINITY : key_float(tk);
+                } else {
+                    bound = key_float(*(volatile uint32_t *)&rs.maxkey);
+                }
+                bool c[U];
+                uint32_t bal[U];
+                int nq = 0;
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    float x[VEC];
+                    F::unpack(v[u], x);
+                    float m = x[0];
+#pragma unroll
+                    for (int j = 1; j < VEC; ++j) m = fmaxf(m, x[j]);
+                    /* raw maximum: NaN only if the whole vector is NaN; the
+                     * penalty only lowers values */
+                    const bool live = base + u * 32 + lane < v1;
+                    c[u] = live && (MODE == kTopK ? m >= bound : scaled_diff(m, bound, a.inv_t) > -15.0f);
+                    bal[u] = __ballot_sync(kFull, c[u]);
+                    nq += __popc(bal[u]);
+                }
+                if (nq) {
+                    if (qfill + nq > kQueueCap) break;  // drain, then redo this batch
+                    const uint32_t id0 = (uint32_t)(g.head + (base + lane) * VEC);
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        if (c[u]) {
+                            const int p = qfill + __popc(bal[u] & lanemask_lt());
+                            st_vec(wq + p, v[u]);
+                            wqid[p] = id0 + (uint32_t)(u * 32 * VEC);
+                        }
+                        qfill += __popc(bal[u]);
+                    }
+                }
+            }
+            if (qfill > 0) {
+                __syncwarp();
+                if (MODE == kTopK) tau_w = topk_drain<T>(a, qfill, tau_w);
+                else full_drain<T>(a, qfill);
+                qfill = 0;
+                __syncwarp();
+                if (MODE == kFullList && (__shfl_sync(kFull, *(volatile int *)&rs.flags, 0) & kOverflow)) break;
+            }
+            if (base >= v1) break;
+        }
+    }
+    row_finish<T, MODE>(a, tau_w, gx, gid);
 }
 
 }  // namespace noel
