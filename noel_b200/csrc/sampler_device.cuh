@@ -850,7 +850,7 @@ __device__ __forceinline__ uint64_t comp_key(uint32_t key, uint32_t id) {
  * rarely and its unrolled network would otherwise crowd the streaming loop.
  */
 template <int R>
-__device__ __noinline__ uint64_t warp_topk_sorted_r(uint32_t *key, uint32_t *id, int n, int K, uint64_t *ladder,
+__device__ __forceinline__ uint64_t warp_topk_sorted_r(uint32_t *key, uint32_t *id, int n, int K, uint64_t *ladder,
                                                    int lad0) {
     constexpr int N = 32 * R;
     const int lane = threadIdx.x & 31;

@@ -329,7 +329,7 @@ __device__ __forceinline__ unsigned long long warp_compact(const RowLayout &L, i
  * insertion, and compaction whenever the buffer fills.  Returns the warp's
  * own threshold. */
 template <typename T>
-__device__ __noinline__ unsigned long long topk_drain(const SampleArgs &a, int n, unsigned long long tau_w) {
+__device__ __forceinline__ unsigned long long topk_drain(const SampleArgs &a, int n, unsigned long long tau_w) {
     constexpr int VEC = Fmt<T>::VEC;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const RowLayout L = row_layout<kTopK>(a, warp);
@@ -369,7 +369,7 @@ __device__ __noinline__ unsigned long long topk_drain(const SampleArgs &a, int n
  * the new maximum cuts when the buffer fills.  Sets kOverflow when the kept
  * list outgrows the buffer. */
 template <typename T>
-__device__ __noinline__ void full_drain(const SampleArgs &a, int n) {
+__device__ __forceinline__ void full_drain(const SampleArgs &a, int n) {
     constexpr int VEC = Fmt<T>::VEC;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const RowLayout L = row_layout<kFullList>(a, warp);
@@ -448,7 +448,7 @@ __device__ __noinline__ uint64_t greedy_take(const SampleArgs &a, uint32_t id0, 
  * K'-th largest gives the row's starting threshold.  Returns the warp's own
  * threshold. */
 template <typename T>
-__device__ __noinline__ unsigned long long row_warmup(const SampleArgs &a, int head, int v0, int v1) {
+__device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, int head, int v0, int v1) {
     using F = Fmt<T>;
     constexpr int NT = kRowThreads, NW = kRowWarps;
     constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U, NE = U * VEC;
@@ -521,7 +521,7 @@ __device__ __noinline__ unsigned long long row_warmup(const SampleArgs &a, int h
 /* Row end (all threads of the block): gather, exactness check, weights and
  * the sequential tail of sampler.c:160-191. */
 template <typename T, int MODE>
-__device__ __noinline__ void row_finish(const SampleArgs &a, unsigned long long tau_w, float gx, uint32_t gid) {
+__device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long long tau_w, float gx, uint32_t gid) {
     constexpr int NT = kRowThreads, NW = kRowWarps;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int row = blockIdx.x;
