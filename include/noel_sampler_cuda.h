@@ -105,6 +105,41 @@ int noel_sampler_sample_batch_noalloc(const noel_sampler_config_t *cfg, const vo
                                       float *d_probs, void *stream);
 
 /*
+ * Vocab-sharded rows: the vocabulary split into column ranges, one per GPU
+ * (rank r holds [v_begin_r, v_begin_r + shard_vocab_r), ranks in ascending
+ * order covering the whole vocabulary).  No counterpart in the reference,
+ * which samples whole rows on the host (sampler.c:80-192); the result equals
+ * noel_sampler_sample on the full row.  Three steps:
+ *
+ *   1. noel_sampler_shard_select on every GPU: for each of the batch rows, the
+ *      shard's K best (global id, penalised logit) by (logit desc, id asc),
+ *      K = noel_sampler_shard_kprime(cfg); its largest penalised logit; flags.
+ *   2. an all-gather of entries [B][K][2] u32, maxima [B] f32 and flags [B]
+ *      i32 across the ranks, in rank order (e.g. ncclAllGather).
+ *   3. noel_sampler_shard_merge on every GPU (identical results everywhere):
+ *      the row's sample from the gathered lists.  A row whose top-k boundary
+ *      cannot be decided from them (a weight tie reaching below the gathered
+ *      entries) gets status 1 and keeps its RNG state: sample it from its full
+ *      row (gather the row's shards) with noel_sampler_sample_batch.
+ *
+ * Supported configs: greedy (temperature <= 1e-4) or 0 < top_k <= 120; others
+ * return NOEL_ERR_UNSUPPORTED (they need every candidate of the row).  The
+ * penalty applies to the history ids inside the shard; d_history holds global
+ * ids.  d_logits points at the shard's first column; ld is its row stride.
+ */
+int noel_sampler_shard_kprime(const noel_sampler_config_t *cfg);
+int noel_sampler_shard_select(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
+                              int batch, int shard_vocab, size_t ld, int v_begin,
+                              const int32_t *d_history, int history_len, size_t hld,
+                              uint32_t *d_entries, float *d_max, int32_t *d_flags, void *stream);
+/* d_entries [n_shards][B][K][2], d_max [n_shards][B], d_flags [n_shards][B];
+ * d_rng [B][2] in/out, d_ids [B], d_probs [B] or NULL, d_status [B]. */
+int noel_sampler_shard_merge(const noel_sampler_config_t *cfg, int n_shards, int batch,
+                             const uint32_t *d_entries, const float *d_max, const int32_t *d_flags,
+                             uint64_t *d_rng, int32_t *d_ids, float *d_probs, int32_t *d_status,
+                             void *stream);
+
+/*
  * Host-buffer form of noel_sampler_sample_batch for callers whose logits are
  * in host memory (the reference engine's layout, src/engine.c:59): copies the
  * rows, histories and states to the device, samples, and copies ids, states

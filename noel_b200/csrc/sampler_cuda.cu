@@ -184,13 +184,32 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, size_t smem_main
     return NOEL_OK;
 }
 
+/* vocab shard output of sample_batch (see SampleArgs) */
+struct ShardOut {
+    int id_off;
+    uint2 *entries;
+    float *maxes;
+    int32_t *flags;
+};
+
+/* entries per row and shard for a config: K' of top-k, 16 for greedy; 0 when
+ * the config needs every candidate (top-k off or above 120) */
+int shard_kprime(const noel_sampler_config_t *cfg) {
+    if (cfg->temperature <= 1e-4f) return 16;
+    if (cfg->top_k <= 0 || cfg->top_k > kWarpKprimeMax - 8) return 0;
+    return pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
+}
+
 int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype, int B, int V,
                  size_t ld, const int32_t *hist, int H, size_t hld, uint64_t *rng, int32_t *ids,
-                 const noel_sample_extras_t *ex, cudaStream_t s, const Workspace *fixed_ws = nullptr) {
+                 const noel_sample_extras_t *ex, cudaStream_t s, const Workspace *fixed_ws = nullptr,
+                 const ShardOut *so = nullptr) {
     if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
     if (B < 0 || V <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", B, V);
     if (B == 0) return ok();
-    if (!logits || !rng || !ids) return fail(NOEL_ERR_INVALID_ARG, "logits, rng and ids are required");
+    if (!logits || (!so && (!rng || !ids))) return fail(NOEL_ERR_INVALID_ARG, "logits, rng and ids are required");
+    if (so && (!so->entries || !so->maxes || !so->flags || so->id_off < 0))
+        return fail(NOEL_ERR_INVALID_ARG, "shard entries, maxima and flags are required, v_begin >= 0");
     if (dtype != NOEL_DTYPE_F32 && dtype != NOEL_DTYPE_BF16) return fail(NOEL_ERR_INVALID_ARG, "dtype %d", dtype);
     if (ld < (size_t)V) return fail(NOEL_ERR_INVALID_ARG, "ld %zu < vocab %d", ld, V);
     const int es = dtype == NOEL_DTYPE_F32 ? 4 : 2;
@@ -239,11 +258,21 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     a.et = c->et;
 
     int mode;
-    if (T <= 1e-4f) mode = kGreedy;  // sampler.c:106
+    if (so) mode = kTopK;            // a vocab shard lists its K' best in every mode
+    else if (T <= 1e-4f) mode = kGreedy;  // sampler.c:106
     else if (cfg->top_k > 0 && cfg->top_k <= kMaxKprime - 8) mode = kTopK;
     else mode = kFullList;
     bool block_kernel = false;
-    if (mode == kTopK) {
+    if (so) {
+        a.kprime = shard_kprime(cfg);
+        if (!a.kprime)
+            return fail(NOEL_ERR_UNSUPPORTED, "a vocab shard needs greedy or 0 < top_k <= %d", kWarpKprimeMax - 8);
+        a.id_off = so->id_off;
+        a.shard_entries = so->entries;
+        a.shard_max = so->maxes;
+        a.shard_flags = so->flags;
+        a.cap = 4 * (a.kprime / 2) < 64 ? 64 : 4 * (a.kprime / 2);
+    } else if (mode == kTopK) {
         a.kprime = pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
         if (a.kprime <= kWarpKprimeMax) {
             const int kw = a.kprime / 2 > 8 ? a.kprime / 2 : 8;  // kept per warp
@@ -556,6 +585,64 @@ struct HostBatchStage {
 };
 thread_local HostBatchStage t_hb;
 }  // namespace
+
+/* ------------------------------------------------------ vocab-sharded rows */
+extern "C" int noel_sampler_shard_kprime(const noel_sampler_config_t *cfg) {
+    if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
+    return shard_kprime(cfg);
+}
+
+extern "C" int noel_sampler_shard_select(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
+                                         int batch, int shard_vocab, size_t ld, int v_begin,
+                                         const int32_t *d_history, int history_len, size_t hld,
+                                         uint32_t *d_entries, float *d_max, int32_t *d_flags, void *stream) {
+    ShardOut so{v_begin, reinterpret_cast<uint2 *>(d_entries), d_max, d_flags};
+    if (reinterpret_cast<uintptr_t>(d_entries) & 7) return fail(NOEL_ERR_INVALID_ARG, "d_entries must be 8-byte aligned");
+    return sample_batch(cfg, d_logits, dtype, batch, shard_vocab, ld, d_history, history_len, hld, nullptr, nullptr,
+                        nullptr, static_cast<cudaStream_t>(stream), nullptr, &so);
+}
+
+extern "C" int noel_sampler_shard_merge(const noel_sampler_config_t *cfg, int n_shards, int batch,
+                                        const uint32_t *d_entries, const float *d_max, const int32_t *d_flags,
+                                        uint64_t *d_rng, int32_t *d_ids, float *d_probs, int32_t *d_status,
+                                        void *stream) {
+    if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
+    if (n_shards <= 0 || batch < 0) return fail(NOEL_ERR_INVALID_ARG, "n_shards %d / batch %d", n_shards, batch);
+    if (batch == 0) return ok();
+    const int K = shard_kprime(cfg);
+    if (!K) return fail(NOEL_ERR_UNSUPPORTED, "a vocab shard needs greedy or 0 < top_k <= %d", kWarpKprimeMax - 8);
+    if (!d_entries || !d_max || !d_flags || !d_rng || !d_ids || !d_status)
+        return fail(NOEL_ERR_INVALID_ARG, "entries, maxima, flags, rng, ids and status are required");
+    if (reinterpret_cast<uintptr_t>(d_entries) & 7) return fail(NOEL_ERR_INVALID_ARG, "d_entries must be 8-byte aligned");
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    const size_t smem = (size_t)kMergeWarps * merge_warp_bytes(n_shards, K);
+    if (smem > c->smem_optin - 1024) return fail(NOEL_ERR_TOO_LARGE, "%d shards x %d entries need %zu B of shared memory",
+                                                 n_shards, K, smem);
+    r = set_smem(c, (const void *)shard_merge_kernel, smem);
+    if (r) return r;
+    MergeArgs m{};
+    m.n_shards = n_shards;
+    m.batch = batch;
+    m.kprime = K;
+    m.entries = reinterpret_cast<const uint2 *>(d_entries);
+    m.maxes = d_max;
+    m.flags = d_flags;
+    m.greedy = cfg->temperature <= 1e-4f;  // sampler.c:106
+    m.inv_t = 1.0f / cfg->temperature;     // sampler.c:132
+    m.top_p = cfg->top_p;
+    m.top_k = cfg->top_k;
+    m.rng = d_rng;
+    m.ids = d_ids;
+    m.probs = d_probs;
+    m.status = d_status;
+    m.et = c->et;
+    const int grid = (batch + kMergeWarps - 1) / kMergeWarps;
+    shard_merge_kernel<<<grid, 32 * kMergeWarps, smem, static_cast<cudaStream_t>(stream)>>>(m);
+    CUDA_TRY(cudaGetLastError());
+    return ok();
+}
 
 extern "C" int noel_sampler_sample_batch_host(const noel_sampler_config_t *cfg, const void *h_logits, int dtype,
                                               int batch, int vocab, size_t ld, const int32_t *h_history,

@@ -85,7 +85,18 @@ struct SampleArgs {
     uint2 *slots;               // exact kernel scratch: nslots x 2 x vocab
     int nslots;
     ExpTable et;
+    /* vocab shard (the row holds columns [id_off, id_off + vocab) of the full
+     * vocabulary): history ids are global; instead of sampling, the kernels
+     * write the shard's kprime best (global id, penalised logit) by (logit
+     * desc, id asc), its largest penalised logit and flags */
+    int id_off;
+    uint2 *shard_entries;       // [B][kprime], id -1 past the listed ones; NULL: no shard output
+    float *shard_max;           // [B] -inf when the shard holds no number
+    int32_t *shard_flags;       // [B] kShardNaN0 | kShardMore
 };
+
+/* shard flags */
+enum { kShardNaN0 = 1, kShardMore = 2 };
 
 /* ---------------------------------------------------------------------- */
 /* scalar helpers                                                          */
@@ -221,13 +232,15 @@ __device__ __forceinline__ int hist_rank(const HistView &h, int t) {
 /* sampler.c:88-93: the window of the row's history, ids in [0, V) only */
 template <int NT>
 __device__ void build_history(const HistView &h, const int32_t *hrow, int first, int H, int V,
-                              int *s_w) {
+                              int *s_w, int id_off = 0) {
     const int W = h.words, G = (W + 7) >> 3;
     for (int i = threadIdx.x; i < W; i += NT) h.bm[i] = 0u;
     __syncthreads();
     for (int i = first + threadIdx.x; i < H; i += NT) {
-        const int t = hrow[i];
-        if (t >= 0 && t < V) atomicOr(&h.bm[t >> 5], 1u << (t & 31));
+        const int g = hrow[i];
+        if (g < id_off || g - id_off >= V) continue;  // sampler.c:95 (ids of this shard)
+        const int t = g - id_off;
+        atomicOr(&h.bm[t >> 5], 1u << (t & 31));
     }
     __syncthreads();
     const int per = (G + NT - 1) / NT;
@@ -250,8 +263,9 @@ __device__ void build_history(const HistView &h, const int32_t *hrow, int first,
     for (int i = threadIdx.x; i < total; i += NT) h.cnt[i] = 0u;
     __syncthreads();
     for (int i = first + threadIdx.x; i < H; i += NT) {
-        const int t = hrow[i];
-        if (t >= 0 && t < V) atomicAdd(&h.cnt[hist_rank(h, t)], 1u);
+        const int g = hrow[i];
+        if (g < id_off || g - id_off >= V) continue;
+        atomicAdd(&h.cnt[hist_rank(h, g - id_off)], 1u);
     }
     __syncthreads();
 }

@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
         s_tau_id = 0xFFFFFFFFu;
         s_maxkey = kKeyNegInf;
     }
-    if (a.penalty) build_history<NT>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w);
+    if (a.penalty) build_history<NT>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w, a.id_off);
     __syncthreads();
 
     const RowGeom g = row_geom<T>(rowp, V);
@@ -513,6 +513,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
 }  // namespace noel
 
 #include "sampler_warp.cuh"
+#include "sampler_shard.cuh"
 
 namespace noel {
 
@@ -621,7 +622,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
         const int row = s_row;
         if (row < 0) break;
         const void *rowp = static_cast<const char *>(a.logits) + (size_t)row * (size_t)a.ld * F::ES;
-        if (pen) build_history<NT>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w);
+        if (pen) build_history<NT>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w, a.id_off);
 
         auto load = [&](int i) -> float {
             float x = F::scalar(rowp, i);
@@ -632,7 +633,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
         float mx = -INFINITY;
         for (int i = tid; i < V; i += NT) {
             const float x = load(i);
-            if (i == 0 && x != x) s_l0nan = 1;
+            if (i == 0 && x != x && a.id_off == 0) s_l0nan = 1;
             mx = fmaxf(mx, x);
         }
         const uint32_t mk = block_max_u32<NT>(mx > -INFINITY ? ord_key(mx) : kKeyNegInf, s_wu);
@@ -648,10 +649,20 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
                 const int i = t0 + tid * IPT + e;
                 wb[e] = 0u;
                 if (i < V) {
-                    const float d = scaled_diff(load(i), M, a.inv_t);
-                    if (d > -15.0f) {
-                        wb[e] = __float_as_uint(ref_weight(d, a.et));
-                        ++c;
+                    const float x = load(i);
+                    if (a.shard_entries) {
+                        /* a vocab shard lists every number by logit (greedy
+                         * rows need them all; ord_key is never 0) */
+                        if (x == x) {
+                            wb[e] = ord_key(x);
+                            ++c;
+                        }
+                    } else {
+                        const float d = scaled_diff(x, M, a.inv_t);
+                        if (d > -15.0f) {
+                            wb[e] = __float_as_uint(ref_weight(d, a.et));
+                            ++c;
+                        }
                     }
                 }
             }
@@ -666,6 +677,20 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
         const bool fb = n == 0;
         uint2 *sorted = slotA;
         if (n > 1) sorted = radix_sort_stable<NT>(slotA, slotB, n, s_h, s_w, &s_skip);
+        if (a.shard_entries) {
+            /* vocab shard: its K' best by (logit desc, id asc) */
+            const int m = min(n, a.kprime);
+            uint2 *out = a.shard_entries + (size_t)row * a.kprime;
+            for (int i = tid; i < a.kprime; i += NT)
+                out[i] = i < m ? make_uint2(sorted[i].y + (uint32_t)a.id_off, __float_as_uint(key_float(~sorted[i].x)))
+                               : make_uint2(0xFFFFFFFFu, 0u);
+            if (tid == 0) {
+                a.shard_max[row] = key_float(mk);
+                a.shard_flags[row] = (s_l0nan ? kShardNaN0 : 0) | (n > a.kprime ? kShardMore : 0);
+            }
+            __syncthreads();
+            continue;
+        }
         if (tid == 0) {
             uint64_t st[2] = {a.rng[2 * (size_t)row], a.rng[2 * (size_t)row + 1]};
             auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float(~sorted[i].x); };

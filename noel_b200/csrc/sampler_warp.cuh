@@ -52,7 +52,7 @@ __device__ __forceinline__ uint32_t hs_hash(uint32_t id) {
 }
 
 template <int NT>
-__device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H, int V) {
+__device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H, int V, int id_off) {
     for (int i = threadIdx.x; i < kBloomWords; i += NT) h.bloom[i] = 0u;
     for (int i = threadIdx.x; i < h.cap; i += NT) {
         h.key[i] = 0u;
@@ -61,8 +61,9 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
     __syncthreads();
     const int bits = __ffs(h.cap) - 1;
     for (int i = first + threadIdx.x; i < H; i += NT) {
-        const int t = hrow[i];
-        if (t < 0 || t >= V) continue;  // sampler.c:95
+        const int gt = hrow[i];
+        if (gt < id_off || gt - id_off >= V) continue;  // sampler.c:95 (ids of this shard)
+        const int t = gt - id_off;
         const uint32_t hh = hs_hash((uint32_t)t);
         const uint32_t b = hh >> 18;  // 14 bits
         atomicOr(&h.bloom[b >> 5], 1u << (b & 31));
@@ -651,6 +652,24 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
         n = a.kprime;
         trunc = true;
     }
+    if (MODE == kTopK && a.shard_entries) {
+        /* vocab shard: its K' best by (logit desc, id asc), its largest
+         * penalised logit, and whether it holds more elements than listed */
+        if (!trunc) {
+            if (a.kprime < 128) warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
+            else warp_topk_sorted_r<8>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
+        }
+        const int m = min(n, a.kprime);
+        uint2 *out = a.shard_entries + (size_t)row * a.kprime;
+        for (int i = lane; i < a.kprime; i += 32)
+            out[i] = i < m ? make_uint2(L.uid[i] + (uint32_t)a.id_off, __float_as_uint(key_float(L.ukey[i])))
+                           : make_uint2(0xFFFFFFFFu, 0u);
+        if (lane == 0) {
+            a.shard_max[row] = m > 0 ? key_float(L.ukey[0]) : -INFINITY;
+            a.shard_flags[row] = (rs.l0nan && a.id_off == 0 ? kShardNaN0 : 0) | (trunc ? kShardMore : 0);
+        }
+        return;
+    }
     float M = Mfull;
     if (MODE == kTopK) {
         uint32_t mk = 0u;
@@ -777,7 +796,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __gri
             const float x0 = F::scalar(rowp, 0);
             rs.l0nan = x0 != x0;  // a NaN at id 0 (the penalty keeps it NaN)
         }
-        if (a.penalty) hs_build<NT>(L.hs, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V);
+        if (a.penalty) hs_build<NT>(L.hs, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, a.id_off);
         __syncthreads();
     }
 
