@@ -339,6 +339,120 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_vocab_sharded(args):
+    """The vocab-sharded workload: every rank holds columns [v_begin, v_begin +
+    width) of all B rows; a step is select on every rank, one NCCL all-gather
+    of the lists, and the merge (plus any full-row fallback).  All ranks
+    sample the same B rows together, so ``value`` is B rows per step time and
+    ``scaling`` is strong."""
+    import torch
+
+    from noel_b200 import sampler as S
+    from noel_b200.sharded import NcclGather, sample_vocab_sharded, sample_vocab_sharded_local, shard_bounds
+    from noel_b200.workloads import WORKLOADS, generate_torch
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    w = WORKLOADS[args.workload]
+    d = generate_torch(w, dev, seed=1)  # the same full rows on every rank
+    b0, width = shard_bounds(w.vocab, world)[rank]
+    shard = d["logits"][:, b0:b0 + width].contiguous()
+    hist, rng = d["history"], d["rng"]
+    del d
+    torch.cuda.empty_cache()
+    cfg = S.make_config(**w.config_kwargs())
+    gather = NcclGather() if world > 1 else None
+    B = shard.shape[0]
+    stream = torch.cuda.current_stream(dev)
+    n_full = [0]
+
+    def step(lg):
+        if world > 1:
+            ids, _, nf = sample_vocab_sharded(cfg, lg, b0, w.vocab, rng, history=hist, gather=gather)
+        else:
+            ids, _, nf = sample_vocab_sharded_local(cfg, lg, [(0, width)], rng, history=hist)
+        n_full[0] += nf
+        return ids
+
+    for _ in range(max(args.warmup, 3)):
+        step(shard)
+    torch.cuda.synchronize()
+    if args.profile:
+        for _ in range(args.steps):
+            step(shard)
+        torch.cuda.synchronize()
+        return
+    n_full[0] = 0
+    clocks = ClockSampler(local if world > 1 else torch.cuda.current_device())
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(shard)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    t_ms = reduce_max(e0.elapsed_time(e1), world)
+    value = B * args.steps / (t_ms / 1e3)
+
+    kb = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ka = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        S.profile_events(kb[i], ka[i])
+        step(shard)
+    S.profile_events(None, None)
+    torch.cuda.synchronize()
+    k_ms = reduce_max(float(np.mean([b.elapsed_time(a) for b, a in zip(kb, ka)])), world)
+    peak, peak_kind = measured_peak()
+    bytes_per_launch = B * (width * 4 + (hist.shape[1] * 4 if hist is not None else 0))
+    achieved = bytes_per_launch / (k_ms / 1e3) / 1e9
+
+    # end to end: the shard's rows from pinned host memory every step, ids back
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    h_shard = shard.cpu().pin_memory()
+    h_ids = torch.empty(B, dtype=torch.int32).pin_memory()
+    d_shard = torch.empty_like(shard)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        d_shard.copy_(h_shard, non_blocking=True)
+        h_ids.copy_(step(d_shard), non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = reduce_max(time.perf_counter() - t0, world)
+
+    if rank == 0:
+        line = {
+            "metric": f"sampled rows/s at batch {B}×vocab {w.vocab} {w.dtype}, vocab-sharded over {world} GPU(s)",
+            "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(workload_config(w, 1), global_batch=B, batch_per_gpu=B,
+                           parallelism=f"vocab-sharded x{world} ({width} columns per GPU)",
+                           l2=f"no flush: {B * width * 4 / 1e6:.0f} MB of logits per GPU per step"),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "sample_rows_kernel (shard select)",
+                         "kernel_ms": k_ms, "bytes_per_launch": bytes_per_launch,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "cpu_baseline": None,
+            "e2e": {"value": B * e2e_steps / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": B * width * 4,
+                    "d2h_bytes_per_step": B * 4, "steps": e2e_steps,
+                    "api": "noel_b200.sharded (select, NCCL all-gather, merge) from pinned host shards"},
+            "rows_from_full_rows": n_full[0],
+            "clocks": clk,
+            "gpu_launches": 3 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -353,6 +467,8 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "vocab_sharded":
+        run_vocab_sharded(args)
     else:
         run_ours(args)
 

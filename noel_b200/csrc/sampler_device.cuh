@@ -339,52 +339,6 @@ __device__ __forceinline__ V8 ld_stream(const V8 *p) {
     return r;
 }
 
-/* ---------------------------------------------------------------------- */
-/* 1-D bulk copies (TMA) into shared memory, completed on an mbarrier       */
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_init_fence() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-/* order earlier generic-proxy reads of a stage before the async-proxy write that reuses it */
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-/* global -> shared, bytes a multiple of 16, both addresses 16-byte aligned; no multicast */
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-/* bounded wait: false after kWaitTries unsuccessful polls (each poll may
- * suspend the thread for a while), so a lost copy ends as an error, not a hang */
-constexpr uint32_t kWaitTries = 1u << 22;
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitTries; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
-
 /* Row geometry: scalar head until 32-byte alignment, vector body, scalar tail. */
 struct RowGeom {
     int head, nvec, tail0, nscalar;

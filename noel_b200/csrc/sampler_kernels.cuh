@@ -9,8 +9,6 @@
 namespace noel {
 
 constexpr int kMainThreads = 256;
-constexpr int kStages = 8;        // shared-memory ring stages per CTA
-constexpr int kChunk = 8192;       // bytes per stage (one bulk copy)
 constexpr int kEPT = 16;         // buffer entries per thread in compactions (cap <= 4096)
 constexpr int kWarmBins = 2048;  // warm-up histogram on the top 11 key bits
 constexpr int kExactThreads = 256;
