@@ -192,6 +192,12 @@ struct ShardOut {
     int32_t *flags;
 };
 
+/* Entries a warp of the single-pass kernel keeps when its buffer fills.  The
+ * row's K' best need no more than K' from one warp; keeping K'/2 makes the
+ * exactness check fail when one warp of four holds half of them, which is
+ * rare for K' >= 64 and frequent for small K', so those keep all K'. */
+int warp_keep(int kprime) { return kprime <= 32 ? kprime : kprime / 2; }
+
 /* entries per row and shard for a config: K' of top-k, 16 for greedy; 0 when
  * the config needs every candidate (top-k off or above 120) */
 int shard_kprime(const noel_sampler_config_t *cfg) {
@@ -271,13 +277,13 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         a.shard_entries = so->entries;
         a.shard_max = so->maxes;
         a.shard_flags = so->flags;
-        a.cap = 4 * (a.kprime / 2) < 64 ? 64 : 4 * (a.kprime / 2);
+        a.kw = warp_keep(a.kprime);
+        a.cap = 4 * a.kw < 64 ? 64 : 4 * a.kw;
     } else if (mode == kTopK) {
         a.kprime = pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
         if (a.kprime <= kWarpKprimeMax) {
-            const int kw = a.kprime / 2 > 8 ? a.kprime / 2 : 8;  // kept per warp
-            const int cap = 4 * kw;                              // per-warp buffer
-            a.cap = cap < 64 ? 64 : cap;
+            a.kw = warp_keep(a.kprime);
+            a.cap = 4 * a.kw < 64 ? 64 : 4 * a.kw;  // per-warp buffer
         } else {
             block_kernel = true;
             const int cap = pow2_at_least(4 * a.kprime);
@@ -308,8 +314,7 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         }
         if (mode != kGreedy) {
             const int nw = kRowWarps;
-            const int kw = a.kprime / 2 > 8 ? a.kprime / 2 : 8;
-            a.ucap = mode == kTopK ? nw * 2 * kw : nw * a.cap;
+            a.ucap = mode == kTopK ? nw * a.kw : nw * a.cap;
             const size_t gather = (size_t)a.ucap * 8 + (size_t)pow2_at_least(a.ucap) * 8;
             const size_t warm = mode == kTopK ? (size_t)2 * kWarpBins * 4 : 0;
             smem_main += (size_t)nw * kQueueCap * (sizeof(V8) + 4) + (size_t)nw * a.cap * 8 +

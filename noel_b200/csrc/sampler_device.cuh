@@ -68,6 +68,7 @@ struct SampleArgs {
     float top_p;
     int top_k;
     int kprime;                 // kept-set size for top-k
+    int kw;                     // entries a warp keeps when it compacts (single-pass kernel)
     int cap;                    // candidate buffer entries
     int hcap;                   // history hash-table slots (single-pass kernel)
     int ucap;                   // gathered-candidate entries (single-pass kernel)
@@ -829,7 +830,11 @@ __device__ __forceinline__ uint64_t warp_topk_sorted_r(uint32_t *key, uint32_t *
         k[r] = i < n ? comp_key(key[i], id[i]) : 0ull;
     }
     warp_sort_desc<R>(k);
-    for (int next = N; next < n; next += N - K) {
+    /* each round replaces the N - K entries below the kept ones; callers pass
+     * K <= N - 32 (the step never drops below 32, so a larger K ends the
+     * loop too) */
+    const int step = N - K > 32 ? N - K : 32;
+    for (int next = N; next < n; next += step) {
 #pragma unroll
         for (int r = 0; r < R; ++r) {
             const int p = lane * R + r;  // sorted position held here

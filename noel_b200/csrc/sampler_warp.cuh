@@ -254,7 +254,7 @@ __device__ __forceinline__ RowLayout row_layout(const SampleArgs &a, int warp) {
     return L;
 }
 
-__device__ __forceinline__ int warp_kw(const SampleArgs &a) { return max(8, a.kprime / 2); }
+__device__ __forceinline__ int warp_kw(const SampleArgs &a) { return a.kw; }
 
 /* ---------------------------------------------------------------------- */
 /* out-of-line paths                                                        */
@@ -283,13 +283,15 @@ __device__ __forceinline__ void buffer_insert(const RowLayout &L, int warp, int 
 
 /* Keep the warp's best kw entries, publish its threshold and ladder, and raise
  * the row's shared filter to the best combination the ladders prove. */
-__device__ __forceinline__ unsigned long long warp_compact(const RowLayout &L, int warp, int capw, int kw) {
+__device__ __forceinline__ unsigned long long warp_compact(const RowLayout &L, int warp, int capw, int kw,
+                                                           int kprime) {
     const int lane = threadIdx.x & 31;
     __syncwarp();
     const int n = min(*(volatile int *)&rs.wfill[warp], capw);
     __syncwarp();
     uint64_t lad[3];
-    const unsigned long long tau_w = warp_topk_sorted_r<4>(L.wkey, L.wid, n, kw, lad, max(1, 2 * kw / kRowWarps));
+    const unsigned long long tau_w =
+        warp_topk_sorted_r<4>(L.wkey, L.wid, n, kw, lad, max(1, kprime / kRowWarps));
     if (lane == 0) {
         rs.wfill[warp] = kw;
         rs.taus[warp] = tau_w;
@@ -297,8 +299,9 @@ __device__ __forceinline__ unsigned long long warp_compact(const RowLayout &L, i
         rs.lad[1][warp] = lad[1];
         rs.lad[2][warp] = lad[2];
         __threadfence_block();
-        /* K' retained elements beat each of: every warp's (2kw/NW)-th, the 4th
-         * largest (kw/2)-th, the 2nd largest kw-th */
+        /* K' retained elements beat each of: every warp's (K'/NW)-th, the 4th
+         * largest (kw/2)-th, the 2nd largest kw-th, and (when kw >= K') the
+         * largest kw-th */
         unsigned long long mn = ~0ull, q4[4] = {0ull, 0ull, 0ull, 0ull}, c1 = 0ull, c2 = 0ull;
         for (int w = 0; w < kRowWarps; ++w) {
             const unsigned long long l0 = *(volatile unsigned long long *)&rs.lad[0][w];
@@ -319,7 +322,7 @@ __device__ __forceinline__ unsigned long long warp_compact(const RowLayout &L, i
             }
         }
         if (kRowWarps < 4) q4[3] = 0ull;
-        atomicMax(&rs.tsh, max(max(mn, q4[3]), c2));
+        atomicMax(&rs.tsh, max(max(mn, q4[3]), max(c2, kw >= kprime ? c1 : 0ull)));
     }
     __syncwarp();
     return tau_w;
@@ -355,7 +358,7 @@ __device__ __forceinline__ unsigned long long topk_drain(const SampleArgs &a, in
             if (!__any_sync(kFull, pend != 0u)) break;
             if (pend) buffer_insert<VEC>(L, warp, capw, x, id0, pend);
             if (!__any_sync(kFull, pend != 0u)) break;
-            tau_w = warp_compact(L, warp, capw, kw);  // the buffer is full
+            tau_w = warp_compact(L, warp, capw, kw, a.kprime);  // the buffer is full
             const unsigned long long te = max(tau_w, *(volatile unsigned long long *)&rs.tsh);
 #pragma unroll
             for (int j = 0; j < VEC; ++j)
@@ -600,7 +603,7 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
             }
             wcount = wn;
         }
-        if (wcount > 2 * kw) {  // keeps the gather within its area
+        if (wcount > kw) {  // each warp brings its best kw to the gather
             tau_w = warp_topk_sorted_r<4>(L.wkey, L.wid, wcount, kw, nullptr, 1);
             wcount = kw;
             wtrunc = true;
@@ -644,7 +647,7 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
             n < a.kprime ? 0ull
                          : (a.kprime < 128 ? warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1)
                                            : warp_topk_sorted_r<8>(L.ukey, L.uid, n, a.kprime, nullptr, 1));
-        if (n < a.kprime || !(T > worst)) {
+        if (n < a.kprime || T < worst) {  // a warp's cut excludes only keys strictly below it
             if (lane == 0) list_exact_row(a, row);
             return;
         }
