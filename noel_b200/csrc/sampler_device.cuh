@@ -1,29 +1,20 @@
 /*
- * Device code of the B200 token sampler (sm_100a).
+ * Device code of the B200 token sampler (sm_100a): the argument block, the
+ * reference's scalar rules, and the warp / block primitives the kernels share.
  *
  * One pass of the reference sampler (Sain-Kai/noel src/sampler.c:80-192) per
  * logits row, restructured for a GPU that streams rows from HBM:
  *
- *   sample_rows_kernel   one CTA per row.  Builds the row's history bitmap
- *                        and per-id occurrence counts in shared memory,
- *                        streams the row once with 128-bit loads, applies the
- *                        penalty on the fly, and keeps a small candidate set
- *                        in shared memory behind a rising threshold:
- *                          greedy  - running argmax (sampler.c:106-116)
- *                          top-k   - the K' = pow2(k+8) largest logits by
- *                                    (logit desc, id asc), compacted by a
- *                                    radix select whenever the buffer fills
- *                          full    - every element that can still pass the
- *                                    -15 cut under the running max
- *                        then computes the reference's weights, sorts them
- *                        by (weight desc, id asc), and runs the sequential
- *                        mass / nucleus / draw loops of sampler.c:160-191.
- *   exact_rows_kernel    rows the first kernel cannot finish exactly (a
- *                        candidate set larger than shared memory, or a tie of
- *                        weights at the top-k boundary reaching below the
- *                        kept set) are redone here in two passes with the
- *                        candidate list in global scratch and a stable radix
- *                        sort, so every row's result is the reference's.
+ *   sample_rows_kernel        (sampler_warp.cuh) one CTA of 4 warps per row;
+ *                             greedy, top-k with k <= 120, and full lists.
+ *   sample_rows_block_kernel  (sampler_kernels.cuh) top-k with k > 120.
+ *   exact_rows_kernel         (sampler_kernels.cuh) rows the others cannot
+ *                             finish exactly (a candidate set larger than
+ *                             shared memory, or a tie of weights at the top-k
+ *                             boundary reaching below the kept set), redone in
+ *                             two passes with the candidate list in global
+ *                             scratch and a stable radix sort.
+ *   shard_merge_kernel        (sampler_shard.cuh) rows split across GPUs.
  *
  * Why selecting by logit is exact: the weight w = expf((x - max) * (1/T)) is
  * non-decreasing in x (fp subtraction and multiplication by a positive are
