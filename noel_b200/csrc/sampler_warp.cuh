@@ -196,6 +196,7 @@ struct RowShared {
     int flags, l0nan, trunc;
     int wcnt[kRowWarps];
     int wfill[kRowWarps];
+    int next;                               // next batch to stream (queued modes)
     int w[kRowWarps + 1];
     float gx[kRowWarps];
     uint32_t gid[kRowWarps];
@@ -771,8 +772,16 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
     }
 }
 
+/* Greedy fits 8 CTAs per SM at 64 registers; the queued modes get 72 (7 per
+ * SM, still one wave for 1024 rows), which removes most of their spills. */
+template <int MODE>
+struct RowOcc {
+    static constexpr int kCtas = MODE == kGreedy ? 8 : 7;
+};
+
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __grid_constant__ SampleArgs a) {
+__global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
+    sample_rows_kernel(const __grid_constant__ SampleArgs a) {
     using F = Fmt<T>;
     constexpr int NT = kRowThreads, NW = kRowWarps;
     constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U, NE = U * VEC;
@@ -798,6 +807,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __gri
             rs.trunc = 0;
             const float x0 = F::scalar(rowp, 0);
             rs.l0nan = x0 != x0;  // a NaN at id 0 (the penalty keeps it NaN)
+            rs.next = NW;
         }
         if (a.penalty) hs_build<NT>(L.hs, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, a.id_off);
         __syncthreads();
@@ -805,7 +815,9 @@ __global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __gri
 
     const RowGeom g = row_geom<T>(rowp, V);
     const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
-    const int per = (g.nvec + NW - 1) / NW;
+    /* greedy: a quarter of the row per warp; queued modes: batches of 32U
+     * vectors, batch w first for warp w, the rest taken as warps free up */
+    const int per = MODE == kGreedy ? (g.nvec + NW - 1) / NW : 32 * U;
     const int v0 = min(g.nvec, warp * per), v1 = min(g.nvec, v0 + per);
 
     float gx = -INFINITY;
@@ -921,21 +933,30 @@ __global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __gri
     } else {
         /* Top-k / full list: load, vector maxima, one comparison; vectors
          * that pass are queued.  When the queue would overflow, the inner
-         * loop stops before that batch, the queue is drained out of line
-         * (one queued vector per lane) and streaming resumes at the same
-         * batch, so no call sits inside the streaming loop.  32 warps per SM
-         * keep enough loads in flight without a register prefetch. */
+         * loop stops before that batch, the queue is drained (one queued
+         * vector per lane) and streaming resumes at the same batch.  Warps
+         * take batches as they free up, so a warp that drained more does
+         * not hold up the row end.  28 warps per SM keep enough loads in
+         * flight without a register prefetch. */
         V8 *const wq = reinterpret_cast<V8 *>(row_smem) + warp * kQueueCap;
         uint32_t *const wqid = reinterpret_cast<uint32_t *>(row_smem + NW * kQueueCap * sizeof(V8)) + warp * kQueueCap;
         int qfill = 0;  // warp-uniform
-        int base = v0;
+        const int nbat = (g.nvec + 32 * U - 1) / (32 * U);
+        int cur = warp;   // batch being streamed (warp-uniform)
+        int nextb = -1;   // the batch after it, once taken
         for (;;) {
-            for (; base < v1; base += 32 * U) {
+            while (cur < nbat) {
+                const int base = cur * 32 * U, end = min(g.nvec, base + 32 * U);
                 V8 v[U];
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int vi = base + u * 32 + lane;
-                    if (vi < v1) v[u] = ld_stream(vbase + vi);
+                    if (vi < end) v[u] = ld_stream(vbase + vi);
+                }
+                if (nextb < 0) {  // take the following batch while the loads fly
+                    int t = 0;
+                    if (lane == 0) t = atomicAdd(&rs.next, 1);
+                    nextb = __shfl_sync(kFull, t, 0);
                 }
                 float bound;  // raw maxima below it cannot pass
                 if (MODE == kTopK) {
@@ -957,7 +978,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __gri
                     for (int j = 1; j < VEC; ++j) m = fmaxf(m, x[j]);
                     /* raw maximum: NaN only if the whole vector is NaN; the
                      * penalty only lowers values */
-                    const bool live = base + u * 32 + lane < v1;
+                    const bool live = base + u * 32 + lane < end;
                     c[u] = live && (MODE == kTopK ? m >= bound : scaled_diff(m, bound, a.inv_t) > -15.0f);
                     bal[u] = __ballot_sync(kFull, c[u]);
                     nq += __popc(bal[u]);
@@ -975,6 +996,8 @@ __global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __gri
                         qfill += __popc(bal[u]);
                     }
                 }
+                cur = nextb;
+                nextb = -1;
             }
             if (qfill > 0) {
                 __syncwarp();
@@ -984,7 +1007,7 @@ __global__ void __launch_bounds__(kRowThreads, 8) sample_rows_kernel(const __gri
                 __syncwarp();
                 if (MODE == kFullList && (__shfl_sync(kFull, *(volatile int *)&rs.flags, 0) & kOverflow)) break;
             }
-            if (base >= v1) break;
+            if (cur >= nbat) break;
         }
     }
     row_finish<T, MODE>(a, tau_w, gx, gid);
