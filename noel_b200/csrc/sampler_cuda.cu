@@ -303,14 +303,14 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     if (block_kernel) {
         smem_main = hist_bytes + (size_t)a.cap * 8 + kWarmBins * 4;
     } else {
-        /* single-pass kernel: Bloom filter + (id, count) table of the window,
+        /* single-pass kernel: bitmap of 8-id blocks + (id, count) table of the window,
          * per-warp buffers, and one area reused by the warm-up histogram and
          * the row-end gather (keys, ids, then the sort keys) */
         smem_main = 0;
         if (a.penalty) {
             const int win = H - a.hist_start > 1 ? H - a.hist_start : 1;
             a.hcap = pow2_at_least(2 * win > 64 ? 2 * win : 64);
-            smem_main += (size_t)kBloomWords * 4 + (size_t)a.hcap * 8;
+            smem_main += (size_t)((hs_blk_words(V) + 3) & ~3) * 4 + (size_t)a.hcap * 8;
         }
         if (mode != kGreedy) {
             const int nw = kRowWarps;

@@ -5,7 +5,7 @@
  * memory footprint small enough for eight CTAs per SM, so the per-row phases
  * of one CTA (history set-up, warm-up, finish) overlap the streaming of others.
  *
- * Row start: the window of the row's history becomes a Bloom filter and an
+ * Row start: the window of the row's history becomes a bitmap of 8-id blocks and an
  * open-addressing table of (id, occurrences) (sampler.c:87-93).
  * Streaming: warp w reads its quarter of the row with 256-bit
  * ld.global.nc.L1::no_allocate.L2::evict_first loads (one batch prefetched),
@@ -35,17 +35,18 @@ namespace noel {
 constexpr int kRowWarps = 4;  // warps streaming one row
 constexpr int kRowThreads = 32 * kRowWarps;
 constexpr int kWarpBins = 512;    // per level of the warm-up histogram (9 key bits)
-constexpr int kBloomWords = 512;  // 16384-bit Bloom filter of the history ids
 
 /* ---------------------------------------------------------------------- */
-/* the row's history: Bloom filter + open-addressing (id -> occurrences)    */
+/* the row's history: a bitmap of 8-id blocks + open addressing (id -> n)   */
 
 struct HistSet {
-    uint32_t *bloom;  // kBloomWords
+    uint32_t *blk;    // bit b: some history id in [8b, 8b + 8); (V + 255) / 256 words
     uint32_t *key;    // cap: id + 1, 0 = empty
     uint32_t *cnt;    // cap: occurrences in the window
     int cap;          // power of two >= 2 x window
 };
+
+__host__ __device__ inline int hs_blk_words(int V) { return (V + 255) / 256; }
 
 __device__ __forceinline__ uint32_t hs_hash(uint32_t id) {
     return id * 0x9E3779B1u;  // Fibonacci hashing
@@ -53,7 +54,7 @@ __device__ __forceinline__ uint32_t hs_hash(uint32_t id) {
 
 template <int NT>
 __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H, int V, int id_off) {
-    for (int i = threadIdx.x; i < kBloomWords; i += NT) h.bloom[i] = 0u;
+    for (int i = threadIdx.x; i < hs_blk_words(V); i += NT) h.blk[i] = 0u;
     for (int i = threadIdx.x; i < h.cap; i += NT) {
         h.key[i] = 0u;
         h.cnt[i] = 0u;
@@ -64,10 +65,8 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
         const int gt = hrow[i];
         if (gt < id_off || gt - id_off >= V) continue;  // sampler.c:95 (ids of this shard)
         const int t = gt - id_off;
-        const uint32_t hh = hs_hash((uint32_t)t);
-        const uint32_t b = hh >> 18;  // 14 bits
-        atomicOr(&h.bloom[b >> 5], 1u << (b & 31));
-        uint32_t p = bits ? (hh >> (32 - bits)) : 0u;
+        atomicOr(&h.blk[t >> 8], 1u << ((t >> 3) & 31));
+        uint32_t p = bits ? (hs_hash((uint32_t)t) >> (32 - bits)) : 0u;
         for (int probe = 0; probe < h.cap; ++probe) {
             const uint32_t prev = atomicCAS(&h.key[p], 0u, (uint32_t)t + 1u);
             if (prev == 0u || prev == (uint32_t)t + 1u) {
@@ -82,11 +81,9 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
 
 /* occurrences of id in the window (0 if none) */
 __device__ __forceinline__ uint32_t hs_count(const HistSet &h, uint32_t id) {
-    const uint32_t hh = hs_hash(id);
-    const uint32_t b = hh >> 18;
-    if (!((h.bloom[b >> 5] >> (b & 31)) & 1u)) return 0u;
+    if (!((h.blk[id >> 8] >> ((id >> 3) & 31)) & 1u)) return 0u;
     const int bits = __ffs(h.cap) - 1;
-    uint32_t p = bits ? (hh >> (32 - bits)) : 0u;
+    uint32_t p = bits ? (hs_hash(id) >> (32 - bits)) : 0u;
     for (int probe = 0; probe < h.cap; ++probe) {
         const uint32_t k = h.key[p];
         if (k == id + 1u) return h.cnt[p];
@@ -96,9 +93,14 @@ __device__ __forceinline__ uint32_t hs_count(const HistSet &h, uint32_t id) {
     return 0u;
 }
 
-/* the penalty on N consecutive ids starting at id0 (sampler.c:93-102) */
+/* the penalty on N consecutive ids starting at id0 (sampler.c:93-102): one or
+ * two bitmap words say whether any of them is in the window */
 template <int N>
 __device__ __forceinline__ void hs_penalize(const HistSet &h, uint32_t id0, float *x, float rep) {
+    const uint32_t b0 = id0 >> 3, b1 = (id0 + N - 1) >> 3;  // at most 3 blocks
+    uint32_t any = 0u;
+    for (uint32_t bb = b0; bb <= b1; ++bb) any |= (h.blk[bb >> 5] >> (bb & 31)) & 1u;
+    if (!any) return;
 #pragma unroll
     for (int j = 0; j < N; ++j) {
         const uint32_t c = hs_count(h, id0 + j);
@@ -231,8 +233,8 @@ __device__ __forceinline__ RowLayout row_layout(const SampleArgs &a, int warp) {
     }
     L.hs = HistSet{nullptr, nullptr, nullptr, 0};
     if (a.penalty) {
-        L.hs.bloom = reinterpret_cast<uint32_t *>(sp);
-        sp += kBloomWords * 4;
+        L.hs.blk = reinterpret_cast<uint32_t *>(sp);
+        sp += ((hs_blk_words(a.vocab) + 3) & ~3) * 4;  // keeps 16-byte alignment
         L.hs.cap = a.hcap;
         L.hs.key = reinterpret_cast<uint32_t *>(sp);
         sp += a.hcap * 4;
