@@ -114,14 +114,19 @@ int workspace(DeviceCtx *c, cudaStream_t s, int rows, int vocab, Workspace **out
         *out = &w;
         return NOEL_OK;
     }
+    /* grow to cover both the old and the new shape, so calls that alternate
+     * between shapes (a split row and its whole-row fallback) settle at once */
+    int rc = rows > 1 ? rows : 1, vc = vocab, ns = nslots > 1 ? nslots : 1;
     if (w.counters) {
+        rc = rc > w.rows_cap ? rc : w.rows_cap;
+        vc = vc > w.vocab_cap ? vc : w.vocab_cap;
+        ns = ns > w.nslots ? ns : w.nslots;
         CUDA_TRY(cudaStreamSynchronize(s));
         cudaFree(w.counters);
         cudaFree(w.rows);
         cudaFree(w.slots);
         w = Workspace{};
     }
-    const int rc = rows > 1 ? rows : 1, vc = vocab, ns = nslots > 1 ? nslots : 1;
     CUDA_TRY(cudaMalloc(&w.counters, 4 * sizeof(int32_t)));
     CUDA_TRY(cudaMemset(w.counters, 0, 4 * sizeof(int32_t)));
     CUDA_TRY(cudaMalloc(&w.rows, (size_t)rc * sizeof(int32_t)));
@@ -190,6 +195,7 @@ struct ShardOut {
     uint2 *entries;
     float *maxes;
     int32_t *flags;
+    int split = 0, split_vocab = 0;  // row splitting (see SampleArgs)
 };
 
 /* Entries a warp of the single-pass kernel keeps when its buffer fills.  The
@@ -214,7 +220,7 @@ int shard_kprime(const noel_sampler_config_t *cfg) {
 int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype, int B, int V,
                  size_t ld, const int32_t *hist, int H, size_t hld, uint64_t *rng, int32_t *ids,
                  const noel_sample_extras_t *ex, cudaStream_t s, const Workspace *fixed_ws = nullptr,
-                 const ShardOut *so = nullptr) {
+                 const ShardOut *so = nullptr, const int32_t *gate = nullptr) {
     if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
     if (B < 0 || V <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", B, V);
     if (B == 0) return ok();
@@ -267,6 +273,7 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         if (ex->write_back && a.penalty) a.wb = const_cast<float *>(static_cast<const float *>(logits));
     }
     a.et = c->et;
+    a.gate = gate;
 
     int mode;
     if (so) mode = kTopK;            // a vocab shard lists its K' best in every mode
@@ -282,6 +289,8 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         a.shard_entries = so->entries;
         a.shard_max = so->maxes;
         a.shard_flags = so->flags;
+        a.split = so->split;
+        a.split_vocab = so->split_vocab;
         a.kw = warp_keep(a.kprime);
         a.cap = warp_buffer(a.kw);
     } else if (mode == kTopK) {
@@ -363,8 +372,14 @@ struct Staging {
     int32_t *d_list = nullptr;
     float *d_listw = nullptr;
     int list_cap = 0;
+    void *d_split = nullptr;  // row split: lists, maxima, flags, status
+    size_t split_cap = 0;
+    void *h_pin = nullptr;    // pinned: ids + stats, RNG state, list ids and weights
+    size_t pin_cap = 0;
     ~Staging() {
         if (dev >= 0) {
+            cudaFreeHost(h_pin);
+            cudaFree(d_split);
             cudaFree(d_logits);
             cudaFree(d_hist);
             cudaFree(d_rng);
@@ -385,6 +400,77 @@ int grow(void **p, size_t *cap, size_t need) {
     CUDA_TRY(cudaMalloc(p, need));
     *cap = need;
     return NOEL_OK;
+}
+
+/* sampler.c:87-103 on the caller's host row: the penalty written back in
+ * place, one application per occurrence in the window, in history order */
+void host_penalize(float *logits, int V, const int32_t *hist, int H, const noel_sampler_config_t *cfg) {
+    const int w = cfg->repetition_window;
+    const int start = (w > 0 && w < H) ? H - w : 0;
+    const float rep = cfg->repetition_penalty;
+    for (int i = start; i < H; ++i) {
+        const int t = hist[i];
+        if (t < 0 || t >= V) continue;
+        logits[t] = logits[t] > 0.0f ? logits[t] / rep : logits[t] * rep;
+    }
+}
+
+/* One row split into column ranges, each selected by its own CTA (the
+ * vocab-shard select on one GPU), then merged: a single row's latency is set
+ * by S CTAs streaming V / S columns instead of one CTA streaming V.  The
+ * merge leaves *d_status = 1 (and the RNG state untouched) for a row it
+ * cannot decide; the caller then samples the whole row. */
+int sample_row_split(const noel_sampler_config_t *cfg, const float *d_row, int V, const int32_t *d_hist, int H,
+                     uint64_t *d_rng, int32_t *d_out, const noel_sample_extras_t *ex, Staging &st, cudaStream_t s,
+                     int32_t **d_status) {
+    const int K = shard_kprime(cfg);
+    int S = V / 16384;
+    S = S < 2 ? 2 : (S > 16 ? 16 : S);
+    int sw = (V + S - 1) / S;
+    sw = (sw + 63) & ~63;  // 256-byte aligned ranges
+    S = (V + sw - 1) / sw;
+    const size_t eb = (size_t)S * K * sizeof(uint2);
+    if (grow(&st.d_split, &st.split_cap, eb + (size_t)S * 8 + 16)) return NOEL_ERR_CUDA;
+    uint2 *entries = static_cast<uint2 *>(st.d_split);
+    float *maxes = reinterpret_cast<float *>(static_cast<char *>(st.d_split) + eb);
+    int32_t *flags = reinterpret_cast<int32_t *>(maxes + S);
+    int32_t *status = flags + S;
+    ShardOut so{0, entries, maxes, flags, S, V};
+    int r = sample_batch(cfg, d_row, NOEL_DTYPE_F32, S, sw, (size_t)V, d_hist, H, (size_t)H, nullptr, nullptr,
+                         nullptr, s, nullptr, &so);
+    if (r) return r;
+    DeviceCtx *c = nullptr;
+    r = device_ctx(&c);
+    if (r) return r;
+    const size_t smem = (size_t)kMergeWarps * merge_warp_bytes(S, K);
+    r = set_smem(c, (const void *)shard_merge_kernel, smem);
+    if (r) return r;
+    MergeArgs m{};
+    m.n_shards = S;
+    m.batch = 1;
+    m.kprime = K;
+    m.es = 1;  // the select wrote list (row b, range q) at b * S + q
+    m.eb = S;
+    m.entries = entries;
+    m.maxes = maxes;
+    m.flags = flags;
+    m.greedy = cfg->temperature <= 1e-4f;  // sampler.c:106
+    m.inv_t = 1.0f / cfg->temperature;     // sampler.c:132
+    m.top_p = cfg->top_p;
+    m.top_k = cfg->top_k;
+    m.rng = d_rng;
+    m.ids = d_out;
+    m.status = status;
+    m.list_ids = ex->d_list_ids;
+    m.list_probs = ex->d_list_probs;
+    m.list_len = ex->d_list_ids ? ex->list_len : 0;
+    m.list_weights = ex->list_weights;
+    m.stats = ex->d_stats;
+    m.et = c->et;
+    shard_merge_kernel<<<1, 32 * kMergeWarps, smem, s>>>(m);
+    CUDA_TRY(cudaGetLastError());
+    *d_status = status;
+    return ok();
 }
 
 bool is_device_ptr(const void *p) {
@@ -505,7 +591,11 @@ extern "C" int32_t noel_sampler_sample(noel_sampler_t *sampler, float *logits, i
             d_hist = st.d_hist;
         }
     }
-    const int list = sampler->candidate_capacity < 4096 ? sampler->candidate_capacity : 4096;
+    /* the drawn-from list: at most top_k entries when top-k applies */
+    const noel_sampler_config_t &cf = sampler->config;
+    int list = sampler->candidate_capacity < 4096 ? sampler->candidate_capacity : 4096;
+    if (cf.temperature <= 1e-4f) list = list < 1 ? list : 1;
+    else if (cf.top_k > 0 && cf.top_k < list) list = cf.top_k;
     if (list > st.list_cap) {
         cudaFree(st.d_list);
         cudaFree(st.d_listw);
@@ -523,31 +613,65 @@ extern "C" int32_t noel_sampler_sample(noel_sampler_t *sampler, float *logits, i
         fail(NOEL_ERR_CUDA, "state copy failed");
         return 0;
     }
+    /* the penalised entries go back to a host row from the host (the same
+     * fp32 operations, without copying the row back); a device row is
+     * written on the device */
+    const bool host_wb = penalty && !dev_logits && !is_device_ptr(history);
     noel_sample_extras_t ex{};
     ex.d_list_ids = list > 0 ? st.d_list : nullptr;
     ex.d_list_probs = list > 0 ? st.d_listw : nullptr;
     ex.list_len = list;
     ex.list_weights = 1;
     ex.d_stats = st.d_out + 4;
-    ex.write_back = penalty ? 1 : 0;
-    if (sample_batch(&sampler->config, d_row, NOEL_DTYPE_F32, 1, vocab_size, (size_t)vocab_size, d_hist,
-                     penalty ? history_len : 0, (size_t)history_len, st.d_rng, st.d_out, &ex, s))
+    ex.write_back = penalty && !host_wb ? 1 : 0;
+    /* long rows of greedy / top-k <= 120 configs: split over many CTAs */
+    const bool split = shard_kprime(&sampler->config) > 0 && vocab_size >= 32768 && !ex.write_back;
+    int32_t *d_status = nullptr;
+    const int hl = penalty ? history_len : 0;
+    if (split) {
+        /* select + merge, then the whole row behind a device gate: it runs
+         * only when the merge left the row undecided (a weight tie at the
+         * top-k boundary; the RNG state is untouched then) */
+        if (sample_row_split(&sampler->config, d_row, vocab_size, d_hist, hl, st.d_rng, st.d_out, &ex, st, s,
+                             &d_status) ||
+            sample_batch(&sampler->config, d_row, NOEL_DTYPE_F32, 1, vocab_size, (size_t)vocab_size, d_hist, hl,
+                         (size_t)history_len, st.d_rng, st.d_out, &ex, s, nullptr, nullptr, d_status))
+            return 0;
+    } else if (sample_batch(&sampler->config, d_row, NOEL_DTYPE_F32, 1, vocab_size, (size_t)vocab_size, d_hist, hl,
+                            (size_t)history_len, st.d_rng, st.d_out, &ex, s)) {
         return 0;
-    int32_t out[8];
-    std::vector<int32_t> lid(list > 0 ? list : 0);
-    std::vector<float> lw(list > 0 ? list : 0);
-    cudaMemcpyAsync(out, st.d_out, sizeof(out), cudaMemcpyDeviceToHost, s);
-    cudaMemcpyAsync(sampler->rng_state, st.d_rng, 16, cudaMemcpyDeviceToHost, s);
-    if (list > 0) {
-        cudaMemcpyAsync(lid.data(), st.d_list, (size_t)list * 4, cudaMemcpyDeviceToHost, s);
-        cudaMemcpyAsync(lw.data(), st.d_listw, (size_t)list * 4, cudaMemcpyDeviceToHost, s);
     }
-    if (penalty && !dev_logits) cudaMemcpyAsync(logits, d_row, row_bytes, cudaMemcpyDeviceToHost, s);
+    /* results through one pinned block, one synchronisation */
+    const size_t pin_need = 64 + (size_t)(list > 0 ? list : 0) * 8;
+    if (st.pin_cap < pin_need) {
+        cudaFreeHost(st.h_pin);
+        st.h_pin = nullptr;
+        st.pin_cap = 0;
+        if (cudaHostAlloc(&st.h_pin, pin_need, cudaHostAllocDefault) != cudaSuccess) {
+            fail(NOEL_ERR_CUDA, "pinned staging allocation failed");
+            return 0;
+        }
+        st.pin_cap = pin_need;
+    }
+    int32_t *out = static_cast<int32_t *>(st.h_pin);                         // id, stats[4]
+    uint64_t *rng_out = reinterpret_cast<uint64_t *>(static_cast<char *>(st.h_pin) + 32);
+    int32_t *lid = reinterpret_cast<int32_t *>(static_cast<char *>(st.h_pin) + 64);
+    float *lw = reinterpret_cast<float *>(lid + (list > 0 ? list : 0));
+    cudaMemcpyAsync(out, st.d_out, 8 * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(rng_out, st.d_rng, 16, cudaMemcpyDeviceToHost, s);
+    if (list > 0) {
+        cudaMemcpyAsync(lid, st.d_list, (size_t)list * 4, cudaMemcpyDeviceToHost, s);
+        cudaMemcpyAsync(lw, st.d_listw, (size_t)list * 4, cudaMemcpyDeviceToHost, s);
+    }
+    if (ex.write_back && !dev_logits) cudaMemcpyAsync(logits, d_row, row_bytes, cudaMemcpyDeviceToHost, s);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
         fail(NOEL_ERR_CUDA, "sampling failed: %s", cudaGetErrorString(e));
         return 0;
     }
+    sampler->rng_state[0] = rng_out[0];
+    sampler->rng_state[1] = rng_out[1];
+    if (host_wb) host_penalize(logits, vocab_size, history, history_len, &sampler->config);
     const int nfinal = out[4 + NOEL_STAT_N_FINAL];
     for (int i = 0; i < list && i < nfinal; ++i) {
         sampler->candidates[i].id = lid[i];
@@ -636,6 +760,8 @@ extern "C" int noel_sampler_shard_merge(const noel_sampler_config_t *cfg, int n_
     m.n_shards = n_shards;
     m.batch = batch;
     m.kprime = K;
+    m.es = batch;  // [n_shards][batch] lists, as gathered across ranks
+    m.eb = 1;
     m.entries = reinterpret_cast<const uint2 *>(d_entries);
     m.maxes = d_max;
     m.flags = d_flags;

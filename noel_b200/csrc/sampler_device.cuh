@@ -85,7 +85,35 @@ struct SampleArgs {
     uint2 *shard_entries;       // [B][kprime], id -1 past the listed ones; NULL: no shard output
     float *shard_max;           // [B] -inf when the shard holds no number
     int32_t *shard_flags;       // [B] kShardNaN0 | kShardMore
+    /* split rows (with shard output): kernel row r is columns
+     * [s * vocab, s * vocab + vocab) of caller row r / split, s = r % split,
+     * of a row of split_vocab columns; 0 or 1: rows are the caller's rows */
+    int split, split_vocab;
+    const int32_t *gate;        // when set, the launch does nothing unless *gate != 0
 };
+
+/* where kernel row r lives: element offset, columns, global id of its first
+ * column, history row */
+struct RowSpan {
+    int64_t off;
+    int V, id_off, hrow;
+};
+__device__ __forceinline__ RowSpan row_span(const SampleArgs &a, int r) {
+    RowSpan s;
+    if (a.split > 1) {
+        const int b = r / a.split, q = r - b * a.split;
+        s.off = (int64_t)b * a.ld + (int64_t)q * a.vocab;
+        s.V = min(a.vocab, a.split_vocab - q * a.vocab);
+        s.id_off = a.id_off + q * a.vocab;
+        s.hrow = b;
+    } else {
+        s.off = (int64_t)r * a.ld;
+        s.V = a.vocab;
+        s.id_off = a.id_off;
+        s.hrow = r;
+    }
+    return s;
+}
 
 /* shard flags */
 enum { kShardNaN0 = 1, kShardMore = 2 };

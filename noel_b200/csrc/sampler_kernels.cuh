@@ -55,6 +55,7 @@ __device__ __forceinline__ void list_exact_row(const SampleArgs &a, int row) {
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(const SampleArgs a) {
+    if (a.gate && *a.gate == 0) return;
     using F = Fmt<T>;
     constexpr int NT = kMainThreads;
     constexpr int VEC = F::VEC, U = F::U, NE = U * VEC;
@@ -583,6 +584,7 @@ __device__ uint2 *radix_sort_stable(uint2 *A, uint2 *B, int n, uint32_t *s_h, in
 
 template <typename T>
 __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleArgs a) {
+    if (a.gate && *a.gate == 0) return;  // no row was listed either
     using F = Fmt<T>;
     constexpr int NT = kExactThreads, NW = NT / 32, IPT = 16;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -619,8 +621,10 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
         __syncthreads();
         const int row = s_row;
         if (row < 0) break;
-        const void *rowp = static_cast<const char *>(a.logits) + (size_t)row * (size_t)a.ld * F::ES;
-        if (pen) build_history<NT>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w, a.id_off);
+        const RowSpan span = row_span(a, row);
+        const int Vr = span.V;
+        const void *rowp = static_cast<const char *>(a.logits) + (size_t)span.off * F::ES;
+        if (pen) build_history<NT>(hv, a.hist + (size_t)span.hrow * a.hld, a.hist_start, a.hist_len, Vr, s_w, span.id_off);
 
         auto load = [&](int i) -> float {
             float x = F::scalar(rowp, i);
@@ -629,9 +633,9 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
         };
         /* pass 1: max of the penalised row (sampler.c:119-124) */
         float mx = -INFINITY;
-        for (int i = tid; i < V; i += NT) {
+        for (int i = tid; i < Vr; i += NT) {
             const float x = load(i);
-            if (i == 0 && x != x && a.id_off == 0) s_l0nan = 1;
+            if (i == 0 && x != x && span.id_off == 0) s_l0nan = 1;
             mx = fmaxf(mx, x);
         }
         const uint32_t mk = block_max_u32<NT>(mx > -INFINITY ? ord_key(mx) : kKeyNegInf, s_wu);
@@ -639,14 +643,14 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
 
         /* pass 2: candidates in id order (sampler.c:136-143) as (~weight bits, id) */
         int n = 0;
-        for (int t0 = 0; t0 < V; t0 += NT * IPT) {
+        for (int t0 = 0; t0 < Vr; t0 += NT * IPT) {
             uint32_t wb[IPT];
             int c = 0;
 #pragma unroll
             for (int e = 0; e < IPT; ++e) {
                 const int i = t0 + tid * IPT + e;
                 wb[e] = 0u;
-                if (i < V) {
+                if (i < Vr) {
                     const float x = load(i);
                     if (a.shard_entries) {
                         /* a vocab shard lists every number by logit (greedy
@@ -680,7 +684,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
             const int m = min(n, a.kprime);
             uint2 *out = a.shard_entries + (size_t)row * a.kprime;
             for (int i = tid; i < a.kprime; i += NT)
-                out[i] = i < m ? make_uint2(sorted[i].y + (uint32_t)a.id_off, __float_as_uint(key_float(~sorted[i].x)))
+                out[i] = i < m ? make_uint2(sorted[i].y + (uint32_t)span.id_off, __float_as_uint(key_float(~sorted[i].x)))
                                : make_uint2(0xFFFFFFFFu, 0u);
             if (tid == 0) {
                 a.shard_max[row] = key_float(mk);

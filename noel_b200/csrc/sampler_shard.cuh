@@ -24,9 +24,10 @@ namespace noel {
 
 struct MergeArgs {
     int n_shards, batch, kprime;
-    const uint2 *entries;  // [n_shards][batch][kprime]
-    const float *maxes;    // [n_shards][batch]
-    const int32_t *flags;  // [n_shards][batch]
+    int es, eb;            // list (shard s, row b) is list s * es + b * eb
+    const uint2 *entries;  // lists of kprime entries
+    const float *maxes;    // one per list
+    const int32_t *flags;  // one per list
     int greedy;            // temperature <= 1e-4 (sampler.c:106)
     float inv_t, top_p;
     int top_k;
@@ -34,6 +35,10 @@ struct MergeArgs {
     int32_t *ids;
     float *probs;          // optional
     int32_t *status;       // [batch] 0 decided here, 1 sample from the full row
+    int32_t *list_ids;     // optional [batch][list_len]: the drawn-from list
+    float *list_probs;
+    int list_len, list_weights;
+    int32_t *stats;        // optional [batch][4] (noel_sampler_cuda.h)
     ExpTable et;
 };
 
@@ -62,11 +67,12 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
     bool more = false, nan0 = false;
     float mx = -INFINITY;
     for (int s = 0; s < a.n_shards; ++s) {
-        const int fl = a.flags[(size_t)s * a.batch + row];
+        const size_t li = (size_t)s * a.es + (size_t)row * a.eb;
+        const int fl = a.flags[li];
         more |= (fl & kShardMore) != 0;
         if (s == 0) nan0 = (fl & kShardNaN0) != 0;
-        mx = fmaxf(mx, a.maxes[(size_t)s * a.batch + row]);
-        const uint2 *e = a.entries + ((size_t)s * a.batch + row) * K;
+        mx = fmaxf(mx, a.maxes[li]);
+        const uint2 *e = a.entries + li * K;
         for (int j0 = 0; j0 < K; j0 += 32) {
             const int j = j0 + lane;
             const uint2 v = j < K ? e[j] : make_uint2(0xFFFFFFFFu, 0u);
@@ -89,11 +95,18 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
         for (int i = lane; i < n; i += 32) best = max(best, comp_key(ukey[i], uid[i]));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(kFull, best, o));
+        const int id = (nan0 || n == 0) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)best);
         if (lane == 0) {
-            a.ids[row] = (nan0 || n == 0) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)best);
+            a.ids[row] = id;
             if (a.probs) a.probs[row] = 1.0f;
             a.status[row] = 0;
+            if (a.stats) reinterpret_cast<int4 *>(a.stats)[row] = make_int4(1, 1, 1, NOEL_ROW_GREEDY);
         }
+        if (a.list_ids)
+            for (int i = lane; i < a.list_len; i += 32) {
+                a.list_ids[(size_t)row * a.list_len + i] = i == 0 ? id : -1;
+                if (a.list_probs) a.list_probs[(size_t)row * a.list_len + i] = i == 0 ? 1.0f : 0.0f;
+            }
         return;
     }
 
@@ -144,8 +157,10 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
         if (lane == 0) a.status[row] = 1;
         return;
     }
+    const bool fb = ncand == 0;  // sampler.c:145-149
+    int nfin = 0;
+    float mass = 0.0f;
     if (lane == 0) {
-        const bool fb = ncand == 0;  // sampler.c:145-149
         uint64_t st[2] = {a.rng[2 * (size_t)row], a.rng[2 * (size_t)row + 1]};
         auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float((uint32_t)(sk[i] >> 32)); };
         const TailOut t = run_tail(fb ? 1 : ncand, more_c, a.top_k, a.top_p, st, w);
@@ -154,6 +169,31 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
         a.ids[row] = fb ? 0 : (int)(0xFFFFFFFFu - (uint32_t)sk[t.pos]);
         if (a.probs) a.probs[row] = __fdiv_rn(w(t.pos), t.mass);
         a.status[row] = 0;
+        if (a.stats)
+            reinterpret_cast<int4 *>(a.stats)[row] =
+                make_int4(more_c ? -1 : (fb ? 1 : ncand), t.n_topk, t.n_final, fb ? NOEL_ROW_FALLBACK : 0);
+        nfin = t.n_final;
+        mass = t.mass;
+    }
+    nfin = __shfl_sync(kFull, nfin, 0);
+    mass = __shfl_sync(kFull, mass, 0);
+    if (a.list_ids) {
+        for (int i = lane; i < a.list_len; i += 32) {
+            int id = -1;
+            float p = 0.0f;
+            if (i < nfin) {
+                if (fb) {
+                    id = 0;
+                    p = 1.0f;
+                } else {
+                    id = (int)(0xFFFFFFFFu - (uint32_t)sk[i]);
+                    p = __uint_as_float((uint32_t)(sk[i] >> 32));
+                    if (!a.list_weights) p = __fdiv_rn(p, mass);
+                }
+            }
+            a.list_ids[(size_t)row * a.list_len + i] = id;
+            if (a.list_probs) a.list_probs[(size_t)row * a.list_len + i] = p;
+        }
     }
 }
 

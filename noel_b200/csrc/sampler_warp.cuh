@@ -666,13 +666,14 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
             else warp_topk_sorted_r<8>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
         }
         const int m = min(n, a.kprime);
+        const int id_off = row_span(a, row).id_off;
         uint2 *out = a.shard_entries + (size_t)row * a.kprime;
         for (int i = lane; i < a.kprime; i += 32)
-            out[i] = i < m ? make_uint2(L.uid[i] + (uint32_t)a.id_off, __float_as_uint(key_float(L.ukey[i])))
+            out[i] = i < m ? make_uint2(L.uid[i] + (uint32_t)id_off, __float_as_uint(key_float(L.ukey[i])))
                            : make_uint2(0xFFFFFFFFu, 0u);
         if (lane == 0) {
             a.shard_max[row] = m > 0 ? key_float(L.ukey[0]) : -INFINITY;
-            a.shard_flags[row] = (rs.l0nan && a.id_off == 0 ? kShardNaN0 : 0) | (trunc ? kShardMore : 0);
+            a.shard_flags[row] = (rs.l0nan && id_off == 0 ? kShardNaN0 : 0) | (trunc ? kShardMore : 0);
         }
         return;
     }
@@ -784,14 +785,16 @@ struct RowOcc {
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
     sample_rows_kernel(const __grid_constant__ SampleArgs a) {
+    if (a.gate && *a.gate == 0) return;
     using F = Fmt<T>;
     constexpr int NT = kRowThreads, NW = kRowWarps;
     constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U, NE = U * VEC;
     static_assert(NE == kLaneElems, "sixteen elements per lane and batch");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int row = blockIdx.x;
-    const int V = a.vocab;
-    const void *rowp = static_cast<const char *>(a.logits) + (size_t)row * (size_t)a.ld * F::ES;
+    const RowSpan span = row_span(a, row);
+    const int V = span.V;
+    const void *rowp = static_cast<const char *>(a.logits) + (size_t)span.off * F::ES;
 
     {
         const RowLayout L = row_layout<MODE>(a, warp);
@@ -811,7 +814,7 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
             rs.l0nan = x0 != x0;  // a NaN at id 0 (the penalty keeps it NaN)
             rs.next = NW;
         }
-        if (a.penalty) hs_build<NT>(L.hs, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, a.id_off);
+        if (a.penalty) hs_build<NT>(L.hs, a.hist + (size_t)span.hrow * a.hld, a.hist_start, a.hist_len, V, span.id_off);
         __syncthreads();
     }
 
