@@ -262,26 +262,35 @@ __device__ __forceinline__ int warp_kw(const SampleArgs &a) { return a.kw; }
 /* ---------------------------------------------------------------------- */
 /* out-of-line paths                                                        */
 
-/* Lane-local insertion of the pend elements of x (ids id0 + e) into the
- * warp's buffer; clears pend for the elements that found a slot. */
+/* Insertion of every lane's pend elements of x (ids id0 + e) into the warp's
+ * buffer (all lanes call it): positions from a warp prefix sum of the lanes'
+ * counts, since the warp is its buffer's only writer.  Clears pend for the
+ * elements that found a slot. */
 template <int N>
 __device__ __forceinline__ void buffer_insert(const RowLayout &L, int warp, int capw, const float (&x)[N],
                                               uint32_t id0, uint32_t &pend) {
-    int slot = atomicAdd(&rs.wfill[warp], __popc(pend));
-    uint32_t pp = pend;
-    while (pp) {
-        const int e = __ffs(pp) - 1;
-        pp &= pp - 1;
-        if (slot < capw) {
-            float xv = x[0];
+    const int lane = threadIdx.x & 31;
+    const int cnt = __popc(pend);
+    int incl = cnt;
 #pragma unroll
-            for (int q = 1; q < N; ++q) xv = (q == e) ? x[q] : xv;
-            L.wkey[slot] = ord_key(xv);
-            L.wid[slot] = id0 + (uint32_t)e;
-            pend &= ~(1u << e);
-        }
-        ++slot;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
     }
+    const int total = __shfl_sync(kFull, incl, 31);
+    const int wf = *(volatile int *)&rs.wfill[warp];
+    int pos = wf + incl - cnt;
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+        if (((pend >> j) & 1u) && pos < capw) {
+            L.wkey[pos] = ord_key(x[j]);
+            L.wid[pos] = id0 + (uint32_t)j;
+            pend &= ~(1u << j);
+            ++pos;
+        }
+    __syncwarp();
+    if (lane == 0) rs.wfill[warp] = min(wf + total, capw);
+    __syncwarp();
 }
 
 /* Keep the warp's best kw entries, publish its threshold and ladder, and raise
@@ -359,7 +368,7 @@ __device__ __forceinline__ unsigned long long topk_drain(const SampleArgs &a, in
         }
         for (;;) {
             if (!__any_sync(kFull, pend != 0u)) break;
-            if (pend) buffer_insert<VEC>(L, warp, capw, x, id0, pend);
+            buffer_insert<VEC>(L, warp, capw, x, id0, pend);
             if (!__any_sync(kFull, pend != 0u)) break;
             tau_w = warp_compact(L, warp, capw, kw, a.kprime);  // the buffer is full
             const unsigned long long te = max(tau_w, *(volatile unsigned long long *)&rs.tsh);
@@ -404,7 +413,7 @@ __device__ __forceinline__ void full_drain(const SampleArgs &a, int n) {
         }
         for (;;) {
             if (!__any_sync(kFull, pend != 0u)) break;
-            if (pend) buffer_insert<VEC>(L, warp, capw, x, id0, pend);
+            buffer_insert<VEC>(L, warp, capw, x, id0, pend);
             if (!__any_sync(kFull, pend != 0u)) break;
             __syncwarp();
             int nb = min(*(volatile int *)&rs.wfill[warp], capw);
