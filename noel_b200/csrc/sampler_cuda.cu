@@ -198,11 +198,13 @@ struct ShardOut {
     int split = 0, split_vocab = 0;  // row splitting (see SampleArgs)
 };
 
-/* Entries a warp of the single-pass kernel keeps when its buffer fills.  The
- * row's K' best need no more than K' from one warp; keeping K'/2 makes the
- * exactness check fail when one warp of four holds half of them, which is
- * rare for K' >= 64 and frequent for small K', so those keep all K'. */
-int warp_keep(int kprime) { return kprime <= 32 ? kprime : kprime / 2; }
+/* Entries a warp of the single-pass kernel keeps when its buffer fills.  A
+ * row falls to the two-pass kernel when one warp holds more of the row's K'
+ * best than it keeps; warps take batches dynamically and may stream well over
+ * a quarter of the row, so they keep 3K'/4 (all K' for K' <= 32), which only
+ * a warp streaming most of the row could exceed.  Keeping all K' everywhere
+ * makes compactions frequent and costs more than it saves. */
+int warp_keep(int kprime) { return kprime <= 32 ? kprime : 3 * kprime / 4; }
 
 /* Entries of a warp's candidate buffer: a compaction sorts the buffer and
  * keeps kw, so a small buffer compacts often (the filters rise sooner) and a

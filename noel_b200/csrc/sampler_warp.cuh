@@ -1,30 +1,33 @@
 /*
  * The single-pass sampling kernel for greedy rows, top-k rows with k <= 120
- * and full-list rows (top-k off): one small CTA (4 warps) per row, warps that
- * stream their own slices of the row without block barriers, and a shared-
- * memory footprint small enough for eight CTAs per SM, so the per-row phases
- * of one CTA (history set-up, warm-up, finish) overlap the streaming of others.
+ * and full-list rows (top-k off): one CTA of 4 warps per row, warps that
+ * stream the row without block barriers, and a shared-memory footprint small
+ * enough for 7-8 CTAs per SM, so 1024 rows run in one wave.
  *
- * Row start: the window of the row's history becomes a bitmap of 8-id blocks and an
- * open-addressing table of (id, occurrences) (sampler.c:87-93).
- * Streaming: warp w reads its quarter of the row with 256-bit
- * ld.global.nc.L1::no_allocate.L2::evict_first loads (one batch prefetched),
- * takes the maximum of each vector and only looks at single elements when
- * that raw maximum can pass the current threshold.  The repetition penalty
- * only lowers values (sampler.c:96-100), so it is applied exactly, but only to
- * vectors that can pass.  Thresholds:
- *   top-k  - the K' = pow2(k+8) best (logit desc, id asc).  A block warm-up on
- *            the first batches starts near the K'-th largest; each warp keeps
- *            its own best K'/2 in a shared-memory buffer, compacts it with a
- *            register bitonic sort when it fills and publishes a ladder of its
- *            kept keys; any combination with K' retained keys above it is a
- *            valid filter for every warp.
- *   full   - the -15 cut under the running maximum (sampler.c:137-138).
- *   greedy - the running (value desc, id asc) maximum (sampler.c:106-116).
+ * Row start: the window of the row's history becomes a bitmap of 8-id blocks
+ * and an open-addressing table of (id, occurrences) (sampler.c:87-93).
+ * Streaming: 256-bit ld.global.nc.L1::no_allocate.L2::evict_first loads; each
+ * lane takes the maximum of each vector and only looks at single elements when
+ * that raw maximum can pass the current filter.  The repetition penalty only
+ * lowers values (sampler.c:96-100), so it is applied exactly, but only to
+ * vectors that can pass.
+ *   greedy  - a quarter of the row per warp, one batch prefetched in
+ *             registers; the running (value desc, id asc) maximum
+ *             (sampler.c:106-116).
+ *   top-k   - the K' = pow2(k+8) best (logit desc, id asc).  Warps take
+ *             batches of the row as they free up and queue passing vectors
+ *             in shared memory; a drain tests them element by element, keeps
+ *             the warp's best kw in a shared-memory buffer (register bitonic
+ *             sort when it fills) and publishes a ladder of kept keys; any
+ *             combination with K' retained keys above it is a valid filter
+ *             for every warp.  A block warm-up on the first batches starts
+ *             the filter near the K'-th largest.
+ *   full    - the -15 cut under the running maximum (sampler.c:137-138).
  * Row end: warp 0 gathers the kept keys, selects the K' best, checks that no
  * excluded element could belong to the top k (else the row goes to the
  * two-pass kernel), computes the weights and runs the sequential mass /
- * nucleus / draw loops of sampler.c:160-191.
+ * nucleus / draw loops of sampler.c:160-191; for a vocab shard it writes the
+ * shard's K' best instead.
  */
 #pragma once
 
@@ -302,6 +305,7 @@ __device__ __forceinline__ unsigned long long warp_compact(const RowLayout &L, i
     const int n = min(*(volatile int *)&rs.wfill[warp], capw);
     __syncwarp();
     uint64_t lad[3];
+    /* kw <= 96 (K' <= 128), within a 4-register sort */
     const unsigned long long tau_w =
         warp_topk_sorted_r<4>(L.wkey, L.wid, n, kw, lad, max(1, kprime / kRowWarps));
     if (lane == 0) {
