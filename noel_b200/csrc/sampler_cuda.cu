@@ -201,10 +201,12 @@ struct ShardOut {
 /* Entries a warp of the single-pass kernel keeps when its buffer fills.  A
  * row falls to the two-pass kernel when one warp holds more of the row's K'
  * best than it keeps; warps take batches dynamically and may stream well over
- * a quarter of the row, so they keep 3K'/4 (all K' for K' <= 32), which only
- * a warp streaming most of the row could exceed.  Keeping all K' everywhere
- * makes compactions frequent and costs more than it saves. */
-int warp_keep(int kprime) { return kprime <= 32 ? kprime : 3 * kprime / 4; }
+ * a quarter of the row, so they keep all K' for K' <= 32 and 3K'/4 for
+ * K' = 64, which only a warp streaming most of the row could exceed.  At
+ * K' = 128 (top-k 57..120) half is as safe: a warp's share of the 128 best
+ * stays near 32.  Keeping all K' everywhere makes compactions frequent and
+ * costs more than it saves. */
+int warp_keep(int kprime) { return kprime <= 32 ? kprime : (kprime <= 64 ? 3 * kprime / 4 : kprime / 2); }
 
 /* Entries of a warp's candidate buffer: a compaction sorts the buffer and
  * keeps kw, so a small buffer compacts often (the filters rise sooner) and a

@@ -834,9 +834,19 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
     const RowGeom g = row_geom<T>(rowp, V);
     const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
     /* greedy: a quarter of the row per warp; queued modes: batches of 32U
-     * vectors, batch w first for warp w, the rest taken as warps free up */
+     * vectors handed out by ticket, ticket w first for warp w, the rest taken
+     * as warps free up.  Ticket t names batch (t mod 4) * bq + t / 4: the first
+     * four tickets start at the quarters of the row and later ones walk the
+     * quarters in turn, so the early thresholds see the whole row (tickets
+     * past the row end name no batch). */
+    const int nbat = (g.nvec + 32 * U - 1) / (32 * U), bq = (nbat + 3) / 4;
+    auto ticket_batch = [&](int t) -> int {
+        const int b = (t & 3) * bq + (t >> 2);
+        return (t >> 2) < bq && b < nbat ? b : -1;
+    };
+    const int first_b = MODE == kGreedy ? warp : ticket_batch(warp);
     const int per = MODE == kGreedy ? (g.nvec + NW - 1) / NW : 32 * U;
-    const int v0 = min(g.nvec, warp * per), v1 = min(g.nvec, v0 + per);
+    const int v0 = first_b < 0 ? g.nvec : min(g.nvec, first_b * per), v1 = min(g.nvec, v0 + per);
 
     float gx = -INFINITY;
     uint32_t gid = 0xFFFFFFFFu;
@@ -959,9 +969,18 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
         V8 *const wq = reinterpret_cast<V8 *>(row_smem) + warp * kQueueCap;
         uint32_t *const wqid = reinterpret_cast<uint32_t *>(row_smem + NW * kQueueCap * sizeof(V8)) + warp * kQueueCap;
         int qfill = 0;  // warp-uniform
-        const int nbat = (g.nvec + 32 * U - 1) / (32 * U);
-        int cur = warp;   // batch being streamed (warp-uniform)
-        int nextb = -1;   // the batch after it, once taken
+        auto take = [&]() -> int {  // the next ticket's batch, nbat when none is left
+            for (;;) {
+                int t = 0;
+                if (lane == 0) t = atomicAdd(&rs.next, 1);
+                t = __shfl_sync(kFull, t, 0);
+                if (t >= 4 * bq) return nbat;
+                const int b = ticket_batch(t);
+                if (b >= 0) return b;
+            }
+        };
+        int cur = first_b >= 0 ? first_b : take();  // batch being streamed (warp-uniform)
+        int nextb = -1;                             // the batch after it, once taken
         for (;;) {
             while (cur < nbat) {
                 const int base = cur * 32 * U, end = min(g.nvec, base + 32 * U);
@@ -971,11 +990,7 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
                     const int vi = base + u * 32 + lane;
                     if (vi < end) v[u] = ld_stream(vbase + vi);
                 }
-                if (nextb < 0) {  // take the following batch while the loads fly
-                    int t = 0;
-                    if (lane == 0) t = atomicAdd(&rs.next, 1);
-                    nextb = __shfl_sync(kFull, t, 0);
-                }
+                if (nextb < 0) nextb = take();  // the following batch, while the loads fly
                 float bound;  // raw maxima below it cannot pass
                 if (MODE == kTopK) {
                     const unsigned long long te = max(tau_w, *(volatile unsigned long long *)&rs.tsh);
