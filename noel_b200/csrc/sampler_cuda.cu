@@ -162,13 +162,15 @@ constexpr int kWarpKprimeMax = 128;  // warp-streaming kernel up to k = 120
 constexpr int kCapMax = 4096;
 
 template <typename T>
-int launch_t(const SampleArgs &a0, int mode, bool block_kernel, size_t smem_main, size_t smem_exact, DeviceCtx *c,
-             cudaStream_t s) {
+int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, size_t smem_main, size_t smem_exact,
+             DeviceCtx *c, cudaStream_t s) {
     const void *kmain = nullptr;
     if (block_kernel) kmain = (const void *)sample_rows_block_kernel<T, kTopK>;
-    else if (mode == kGreedy) kmain = (const void *)sample_rows_kernel<T, kGreedy>;
-    else if (mode == kTopK) kmain = (const void *)sample_rows_kernel<T, kTopK>;
-    else kmain = (const void *)sample_rows_kernel<T, kFullList>;
+    else if (mode == kGreedy) kmain = (const void *)sample_rows_kernel<T, kGreedy, 1>;
+    else if (mode == kTopK) kmain = wide ? (const void *)sample_rows_kernel<T, kTopK, 4>
+                                         : (const void *)sample_rows_kernel<T, kTopK, 1>;
+    else kmain = wide ? (const void *)sample_rows_kernel<T, kFullList, 4>
+                      : (const void *)sample_rows_kernel<T, kFullList, 1>;
     const void *kexact = (const void *)exact_rows_kernel<T>;
     int r = set_smem(c, kmain, smem_main);
     if (r) return r;
@@ -177,9 +179,11 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, size_t smem_main
     if (t_ev_before) CUDA_TRY(cudaEventRecord(t_ev_before, s));
     const int grid = a0.batch;  // one CTA per row
     if (block_kernel) sample_rows_block_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
-    else if (mode == kGreedy) sample_rows_kernel<T, kGreedy><<<grid, kRowThreads, smem_main, s>>>(a0);
-    else if (mode == kTopK) sample_rows_kernel<T, kTopK><<<grid, kRowThreads, smem_main, s>>>(a0);
-    else sample_rows_kernel<T, kFullList><<<grid, kRowThreads, smem_main, s>>>(a0);
+    else if (mode == kGreedy) sample_rows_kernel<T, kGreedy, 1><<<grid, kRowThreads, smem_main, s>>>(a0);
+    else if (mode == kTopK && wide) sample_rows_kernel<T, kTopK, 4><<<grid, kRowThreads, smem_main, s>>>(a0);
+    else if (mode == kTopK) sample_rows_kernel<T, kTopK, 1><<<grid, kRowThreads, smem_main, s>>>(a0);
+    else if (wide) sample_rows_kernel<T, kFullList, 4><<<grid, kRowThreads, smem_main, s>>>(a0);
+    else sample_rows_kernel<T, kFullList, 1><<<grid, kRowThreads, smem_main, s>>>(a0);
     CUDA_TRY(cudaGetLastError());
     if (t_ev_after) CUDA_TRY(cudaEventRecord(t_ev_after, s));
     if (mode != kGreedy) {
@@ -221,10 +225,12 @@ int shard_kprime(const noel_sampler_config_t *cfg) {
     return pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
 }
 
+/* B rows of V columns, one CTA per row (or per range of a row, with a shard
+ * output) */
 int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype, int B, int V,
                  size_t ld, const int32_t *hist, int H, size_t hld, uint64_t *rng, int32_t *ids,
                  const noel_sample_extras_t *ex, cudaStream_t s, const Workspace *fixed_ws = nullptr,
-                 const ShardOut *so = nullptr, const int32_t *gate = nullptr) {
+                 const ShardOut *so = nullptr) {
     if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
     if (B < 0 || V <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", B, V);
     if (B == 0) return ok();
@@ -277,7 +283,6 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         if (ex->write_back && a.penalty) a.wb = const_cast<float *>(static_cast<const float *>(logits));
     }
     a.et = c->et;
-    a.gate = gate;
 
     int mode;
     if (so) mode = kTopK;            // a vocab shard lists its K' best in every mode
@@ -318,6 +323,7 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         hist_bytes = (hist_bytes + 15) & ~size_t(15);
     }
     size_t smem_main;
+    bool wide = false;
     if (block_kernel) {
         smem_main = hist_bytes + (size_t)a.cap * 8 + kWarmBins * 4;
     } else {
@@ -332,10 +338,15 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         }
         if (mode != kGreedy) {
             const int nw = kRowWarps;
+            /* a batch too small to fill the GPU at 7 rows per SM streams each
+             * row with batches four times as wide (2 rows per SM) */
+            wide = B <= 2 * c->sms;
+            const int u = (dtype == NOEL_DTYPE_F32 ? 2 : 1) * (wide ? 4 : 1);  // vectors per lane and batch
+            a.qcap = 32 * u > kQueueCap ? 32 * u : kQueueCap;
             a.ucap = mode == kTopK ? nw * a.kw : nw * a.cap;
             const size_t gather = (size_t)a.ucap * 8 + (size_t)pow2_at_least(a.ucap) * 8;
             const size_t warm = mode == kTopK ? (size_t)2 * kWarpBins * 4 : 0;
-            smem_main += (size_t)nw * kQueueCap * (sizeof(V8) + 4) + (size_t)nw * a.cap * 8 +
+            smem_main += (size_t)nw * a.qcap * (sizeof(V8) + 4) + (size_t)nw * a.cap * 8 +
                          (gather > warm ? gather : warm);
         }
     }
@@ -357,8 +368,8 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         a.slots = w->slots;
         a.nslots = w->nslots;
     }
-    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, block_kernel, smem_main, smem_exact, c, s)
-                                : launch_t<uint16_t>(a, mode, block_kernel, smem_main, smem_exact, c, s);
+    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, block_kernel, wide, smem_main, smem_exact, c, s)
+                                : launch_t<uint16_t>(a, mode, block_kernel, wide, smem_main, smem_exact, c, s);
     if (r) return r;
     return ok();
 }
@@ -376,14 +387,11 @@ struct Staging {
     int32_t *d_list = nullptr;
     float *d_listw = nullptr;
     int list_cap = 0;
-    void *d_split = nullptr;  // row split: lists, maxima, flags, status
-    size_t split_cap = 0;
     void *h_pin = nullptr;    // pinned: ids + stats, RNG state, list ids and weights
     size_t pin_cap = 0;
     ~Staging() {
         if (dev >= 0) {
             cudaFreeHost(h_pin);
-            cudaFree(d_split);
             cudaFree(d_logits);
             cudaFree(d_hist);
             cudaFree(d_rng);
@@ -417,64 +425,6 @@ void host_penalize(float *logits, int V, const int32_t *hist, int H, const noel_
         if (t < 0 || t >= V) continue;
         logits[t] = logits[t] > 0.0f ? logits[t] / rep : logits[t] * rep;
     }
-}
-
-/* One row split into column ranges, each selected by its own CTA (the
- * vocab-shard select on one GPU), then merged: a single row's latency is set
- * by S CTAs streaming V / S columns instead of one CTA streaming V.  The
- * merge leaves *d_status = 1 (and the RNG state untouched) for a row it
- * cannot decide; the caller then samples the whole row. */
-int sample_row_split(const noel_sampler_config_t *cfg, const float *d_row, int V, const int32_t *d_hist, int H,
-                     uint64_t *d_rng, int32_t *d_out, const noel_sample_extras_t *ex, Staging &st, cudaStream_t s,
-                     int32_t **d_status) {
-    const int K = shard_kprime(cfg);
-    int S = V / 16384;
-    S = S < 2 ? 2 : (S > 16 ? 16 : S);
-    int sw = (V + S - 1) / S;
-    sw = (sw + 63) & ~63;  // 256-byte aligned ranges
-    S = (V + sw - 1) / sw;
-    const size_t eb = (size_t)S * K * sizeof(uint2);
-    if (grow(&st.d_split, &st.split_cap, eb + (size_t)S * 8 + 16)) return NOEL_ERR_CUDA;
-    uint2 *entries = static_cast<uint2 *>(st.d_split);
-    float *maxes = reinterpret_cast<float *>(static_cast<char *>(st.d_split) + eb);
-    int32_t *flags = reinterpret_cast<int32_t *>(maxes + S);
-    int32_t *status = flags + S;
-    ShardOut so{0, entries, maxes, flags, S, V};
-    int r = sample_batch(cfg, d_row, NOEL_DTYPE_F32, S, sw, (size_t)V, d_hist, H, (size_t)H, nullptr, nullptr,
-                         nullptr, s, nullptr, &so);
-    if (r) return r;
-    DeviceCtx *c = nullptr;
-    r = device_ctx(&c);
-    if (r) return r;
-    const size_t smem = (size_t)kMergeWarps * merge_warp_bytes(S, K);
-    r = set_smem(c, (const void *)shard_merge_kernel, smem);
-    if (r) return r;
-    MergeArgs m{};
-    m.n_shards = S;
-    m.batch = 1;
-    m.kprime = K;
-    m.es = 1;  // the select wrote list (row b, range q) at b * S + q
-    m.eb = S;
-    m.entries = entries;
-    m.maxes = maxes;
-    m.flags = flags;
-    m.greedy = cfg->temperature <= 1e-4f;  // sampler.c:106
-    m.inv_t = 1.0f / cfg->temperature;     // sampler.c:132
-    m.top_p = cfg->top_p;
-    m.top_k = cfg->top_k;
-    m.rng = d_rng;
-    m.ids = d_out;
-    m.status = status;
-    m.list_ids = ex->d_list_ids;
-    m.list_probs = ex->d_list_probs;
-    m.list_len = ex->d_list_ids ? ex->list_len : 0;
-    m.list_weights = ex->list_weights;
-    m.stats = ex->d_stats;
-    m.et = c->et;
-    shard_merge_kernel<<<1, 32 * kMergeWarps, smem, s>>>(m);
-    CUDA_TRY(cudaGetLastError());
-    *d_status = status;
-    return ok();
 }
 
 bool is_device_ptr(const void *p) {
@@ -628,23 +578,12 @@ extern "C" int32_t noel_sampler_sample(noel_sampler_t *sampler, float *logits, i
     ex.list_weights = 1;
     ex.d_stats = st.d_out + 4;
     ex.write_back = penalty && !host_wb ? 1 : 0;
-    /* long rows of greedy / top-k <= 120 configs: split over many CTAs */
-    const bool split = shard_kprime(&sampler->config) > 0 && vocab_size >= 32768 && !ex.write_back;
-    int32_t *d_status = nullptr;
+    /* one row: the single-pass kernel's wide batches (a batch this small
+     * runs at 2 CTAs per SM, each row with four times the loads in flight) */
     const int hl = penalty ? history_len : 0;
-    if (split) {
-        /* select + merge, then the whole row behind a device gate: it runs
-         * only when the merge left the row undecided (a weight tie at the
-         * top-k boundary; the RNG state is untouched then) */
-        if (sample_row_split(&sampler->config, d_row, vocab_size, d_hist, hl, st.d_rng, st.d_out, &ex, st, s,
-                             &d_status) ||
-            sample_batch(&sampler->config, d_row, NOEL_DTYPE_F32, 1, vocab_size, (size_t)vocab_size, d_hist, hl,
-                         (size_t)history_len, st.d_rng, st.d_out, &ex, s, nullptr, nullptr, d_status))
-            return 0;
-    } else if (sample_batch(&sampler->config, d_row, NOEL_DTYPE_F32, 1, vocab_size, (size_t)vocab_size, d_hist, hl,
-                            (size_t)history_len, st.d_rng, st.d_out, &ex, s)) {
+    if (sample_batch(&sampler->config, d_row, NOEL_DTYPE_F32, 1, vocab_size, (size_t)vocab_size, d_hist, hl,
+                     (size_t)history_len, st.d_rng, st.d_out, &ex, s))
         return 0;
-    }
     /* results through one pinned block, one synchronisation */
     const size_t pin_need = 64 + (size_t)(list > 0 ? list : 0) * 8;
     if (st.pin_cap < pin_need) {
@@ -924,8 +863,9 @@ NoAllocDev g_noalloc_dev[64];  // per device ordinal; fixed storage, nothing all
 template <typename T>
 int preset_attrs(DeviceCtx *c) {
     const size_t mx = c->smem_optin;
-    const void *ks[] = {(const void *)sample_rows_kernel<T, kGreedy>, (const void *)sample_rows_kernel<T, kTopK>,
-                        (const void *)sample_rows_kernel<T, kFullList>, (const void *)sample_rows_block_kernel<T, kTopK>,
+    const void *ks[] = {(const void *)sample_rows_kernel<T, kGreedy, 1>, (const void *)sample_rows_kernel<T, kTopK, 1>,
+                        (const void *)sample_rows_kernel<T, kTopK, 4>, (const void *)sample_rows_kernel<T, kFullList, 1>,
+                        (const void *)sample_rows_kernel<T, kFullList, 4>, (const void *)sample_rows_block_kernel<T, kTopK>,
                         (const void *)exact_rows_kernel<T>};
     for (const void *k : ks) {
         cudaFuncAttributes fa;

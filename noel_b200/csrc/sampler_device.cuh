@@ -89,7 +89,7 @@ struct SampleArgs {
      * [s * vocab, s * vocab + vocab) of caller row r / split, s = r % split,
      * of a row of split_vocab columns; 0 or 1: rows are the caller's rows */
     int split, split_vocab;
-    const int32_t *gate;        // when set, the launch does nothing unless *gate != 0
+    int qcap;                   // queued vectors per warp (single-pass kernel, queued modes)
 };
 
 /* where kernel row r lives: element offset, columns, global id of its first

@@ -55,7 +55,6 @@ __device__ __forceinline__ void list_exact_row(const SampleArgs &a, int row) {
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(const SampleArgs a) {
-    if (a.gate && *a.gate == 0) return;
     using F = Fmt<T>;
     constexpr int NT = kMainThreads;
     constexpr int VEC = F::VEC, U = F::U, NE = U * VEC;
@@ -166,12 +165,23 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
             }
         }
         if (a.penalty) {
+            /* Top-k after the warm-up: the penalty only lowers values, so an
+             * element whose raw value is below the current threshold fails
+             * the filter either way and needs no history lookup. */
+            const float ptau = (MODE == kTopK && !(warm && it == 0)) ? key_float(s_tau_key) : -INFINITY;
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int vi = it * per_iter + u * NT + tid;
                 if (vi < g.nvec) {
                     const int id0 = g.head + vi * VEC;
                     uint32_t bits = hist_bits(hv, id0, VEC);
+                    if (MODE == kTopK && bits) {
+                        uint32_t need = 0u;
+#pragma unroll
+                        for (int j = 0; j < VEC; ++j)
+                            if (x[u * VEC + j] >= ptau) need |= 1u << j;
+                        bits &= need;
+                    }
                     while (bits) {
                         const int j = __ffs(bits) - 1;
                         bits &= bits - 1;
@@ -584,7 +594,6 @@ __device__ uint2 *radix_sort_stable(uint2 *A, uint2 *B, int n, uint32_t *s_h, in
 
 template <typename T>
 __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleArgs a) {
-    if (a.gate && *a.gate == 0) return;  // no row was listed either
     using F = Fmt<T>;
     constexpr int NT = kExactThreads, NW = NT / 32, IPT = 16;
     extern __shared__ __align__(16) unsigned char smem[];

@@ -62,9 +62,20 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
     uint32_t *uid = ukey + cap;
     uint64_t *sk = reinterpret_cast<uint64_t *>(uid + cap);
 
+    /* A shard that listed K entries has K elements at or above its K-th, so
+     * the row's K-th best is at least the largest such K-th entry: entries
+     * below that floor cannot make the row's K best and are not gathered. */
+    uint64_t floor_key = 0ull;
+    for (int s = lane; s < a.n_shards; s += 32) {
+        const uint2 v = a.entries[((size_t)s * a.es + (size_t)row * a.eb) * K + (K - 1)];
+        if (v.x != 0xFFFFFFFFu) floor_key = max(floor_key, comp_key(ord_key(__uint_as_float(v.y)), v.x));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) floor_key = max(floor_key, __shfl_xor_sync(kFull, floor_key, o));
+
     /* gather the shards' lists, maxima and flags */
     int n = 0;
-    bool more = false, nan0 = false;
+    bool more = false, nan0 = false, dropped = false;
     float mx = -INFINITY;
     for (int s = 0; s < a.n_shards; ++s) {
         const size_t li = (size_t)s * a.es + (size_t)row * a.eb;
@@ -76,7 +87,9 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
         for (int j0 = 0; j0 < K; j0 += 32) {
             const int j = j0 + lane;
             const uint2 v = j < K ? e[j] : make_uint2(0xFFFFFFFFu, 0u);
-            const bool ok = v.x != 0xFFFFFFFFu;
+            const bool listed = v.x != 0xFFFFFFFFu;
+            const bool ok = listed && comp_key(ord_key(__uint_as_float(v.y)), v.x) >= floor_key;
+            dropped |= listed && !ok;
             const uint32_t bal = __ballot_sync(kFull, ok);
             if (ok) {
                 const int p = n + __popc(bal & lanemask_lt());
@@ -113,7 +126,7 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
     /* the row's K best by (logit desc, id asc), sorted */
     const unsigned long long T = K < 128 ? warp_topk_sorted_r<4>(ukey, uid, n, K, nullptr, 1)
                                          : warp_topk_sorted_r<8>(ukey, uid, n, K, nullptr, 1);
-    const bool trunc = more || n > K;
+    const bool trunc = more || n > K || __any_sync(kFull, dropped);
     const int m = min(n, K);
     const float M = nan0 ? __uint_as_float(0x7FC00000u) : mx;
     int P = 1;

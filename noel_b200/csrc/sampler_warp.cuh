@@ -45,7 +45,8 @@ constexpr int kWarpBins = 512;    // per level of the warm-up histogram (9 key b
 struct HistSet {
     uint32_t *blk;    // bit b: some history id in [8b, 8b + 8); (V + 255) / 256 words
     uint32_t *key;    // cap: id + 1, 0 = empty
-    uint32_t *cnt;    // cap: occurrences in the window
+    uint32_t *val;    // cap: occurrences in the window while building, then the
+                      // penalised logit (float bits)
     int cap;          // power of two >= 2 x window
 };
 
@@ -55,12 +56,17 @@ __device__ __forceinline__ uint32_t hs_hash(uint32_t id) {
     return id * 0x9E3779B1u;  // Fibonacci hashing
 }
 
-template <int NT>
-__device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H, int V, int id_off) {
+/* The window's distinct ids with their occurrence counts, then each id's
+ * penalised logit, computed once per row: the penalty applies per occurrence
+ * (sampler.c:93-102), so an id seen c times takes c dependent roundings, and
+ * the streaming code only substitutes the stored value. */
+template <typename T, int NT>
+__device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H, int V, int id_off,
+                         const void *rowp, float rep) {
     for (int i = threadIdx.x; i < hs_blk_words(V); i += NT) h.blk[i] = 0u;
     for (int i = threadIdx.x; i < h.cap; i += NT) {
         h.key[i] = 0u;
-        h.cnt[i] = 0u;
+        h.val[i] = 0u;
     }
     __syncthreads();
     const int bits = __ffs(h.cap) - 1;
@@ -73,41 +79,50 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
         for (int probe = 0; probe < h.cap; ++probe) {
             const uint32_t prev = atomicCAS(&h.key[p], 0u, (uint32_t)t + 1u);
             if (prev == 0u || prev == (uint32_t)t + 1u) {
-                atomicAdd(&h.cnt[p], 1u);
+                atomicAdd(&h.val[p], 1u);
                 break;
             }
             p = (p + 1) & (uint32_t)(h.cap - 1);
         }
     }
     __syncthreads();
+    for (int s = threadIdx.x; s < h.cap; s += NT) {
+        const uint32_t k = h.key[s];
+        if (k) h.val[s] = __float_as_uint(apply_penalty(Fmt<T>::scalar(rowp, (int)(k - 1u)), h.val[s], rep));
+    }
+    __syncthreads();
 }
 
-/* occurrences of id in the window (0 if none) */
-__device__ __forceinline__ uint32_t hs_count(const HistSet &h, uint32_t id) {
-    if (!((h.blk[id >> 8] >> ((id >> 3) & 31)) & 1u)) return 0u;
+/* the penalised logit of id if id is in the window */
+__device__ __forceinline__ bool hs_find(const HistSet &h, uint32_t id, float &x) {
+    if (!((h.blk[id >> 8] >> ((id >> 3) & 31)) & 1u)) return false;
     const int bits = __ffs(h.cap) - 1;
     uint32_t p = bits ? (hs_hash(id) >> (32 - bits)) : 0u;
     for (int probe = 0; probe < h.cap; ++probe) {
         const uint32_t k = h.key[p];
-        if (k == id + 1u) return h.cnt[p];
-        if (k == 0u) return 0u;
+        if (k == id + 1u) {
+            x = __uint_as_float(h.val[p]);
+            return true;
+        }
+        if (k == 0u) return false;
         p = (p + 1) & (uint32_t)(h.cap - 1);
     }
-    return 0u;
+    return false;
 }
 
 /* the penalty on N consecutive ids starting at id0 (sampler.c:93-102): one or
- * two bitmap words say whether any of them is in the window */
+ * two bitmap words say whether any of them is in the window; an id in it
+ * takes its penalised logit from the table */
 template <int N>
-__device__ __forceinline__ void hs_penalize(const HistSet &h, uint32_t id0, float *x, float rep) {
+__device__ __forceinline__ void hs_penalize(const HistSet &h, uint32_t id0, float *x) {
     const uint32_t b0 = id0 >> 3, b1 = (id0 + N - 1) >> 3;  // at most 3 blocks
     uint32_t any = 0u;
     for (uint32_t bb = b0; bb <= b1; ++bb) any |= (h.blk[bb >> 5] >> (bb & 31)) & 1u;
     if (!any) return;
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-        const uint32_t c = hs_count(h, id0 + j);
-        if (c) x[j] = apply_penalty(x[j], c, rep);
+        float v;
+        if (hs_find(h, id0 + j, v)) x[j] = v;
     }
 }
 
@@ -117,7 +132,7 @@ __device__ void hs_write_back(const SampleArgs &a, const HistSet &h, int row) {
     float *wrow = a.wb + (size_t)row * a.ld;
     for (int s = threadIdx.x; s < h.cap; s += NT) {
         const uint32_t k = h.key[s];
-        if (k) wrow[k - 1] = apply_penalty(wrow[k - 1], h.cnt[s], a.rep);
+        if (k) wrow[k - 1] = __uint_as_float(h.val[s]);
     }
 }
 
@@ -167,7 +182,7 @@ struct WarpFmt<uint16_t> {
     static constexpr int VEC = 16, U = 1;
 };
 constexpr int kLaneElems = 16;
-constexpr int kQueueCap = 64;  // queued vectors per warp (>= the vectors of one batch)
+constexpr int kQueueCap = 64;  // queued vectors per warp at one-wave occupancy (>= the vectors of one batch)
 
 /* one lane's batch, passed by value to the out-of-line paths */
 struct LaneBatch {
@@ -229,10 +244,10 @@ __device__ __forceinline__ RowLayout row_layout(const SampleArgs &a, int warp) {
     L.q = nullptr;
     L.qid = nullptr;
     if (MODE != kGreedy) {
-        L.q = reinterpret_cast<V8 *>(sp) + warp * kQueueCap;
-        sp += NW * kQueueCap * sizeof(V8);
-        L.qid = reinterpret_cast<uint32_t *>(sp) + warp * kQueueCap;
-        sp += NW * kQueueCap * 4;
+        L.q = reinterpret_cast<V8 *>(sp) + warp * a.qcap;
+        sp += NW * a.qcap * sizeof(V8);
+        L.qid = reinterpret_cast<uint32_t *>(sp) + warp * a.qcap;
+        sp += NW * a.qcap * 4;
     }
     L.hs = HistSet{nullptr, nullptr, nullptr, 0};
     if (a.penalty) {
@@ -241,7 +256,7 @@ __device__ __forceinline__ RowLayout row_layout(const SampleArgs &a, int warp) {
         L.hs.cap = a.hcap;
         L.hs.key = reinterpret_cast<uint32_t *>(sp);
         sp += a.hcap * 4;
-        L.hs.cnt = reinterpret_cast<uint32_t *>(sp);
+        L.hs.val = reinterpret_cast<uint32_t *>(sp);
         sp += a.hcap * 4;
     }
     L.wkey = L.wid = L.area = L.ukey = L.uid = nullptr;
@@ -361,7 +376,7 @@ __device__ __forceinline__ unsigned long long topk_drain(const SampleArgs &a, in
         if (i < n) {
             Fmt<T>::unpack(ld_vec(L.q + i), x);
             id0 = L.qid[i];
-            if (a.penalty) hs_penalize<VEC>(L.hs, id0, x, a.rep);
+            if (a.penalty) hs_penalize<VEC>(L.hs, id0, x);
             const unsigned long long te = max(tau_w, *(volatile unsigned long long *)&rs.tsh);
             const uint32_t tk = (uint32_t)(te >> 32);
             const float tau_f = tk == 0u ? -INFINITY : key_float(tk);
@@ -402,7 +417,7 @@ __device__ __forceinline__ void full_drain(const SampleArgs &a, int n) {
         if (i < n) {
             Fmt<T>::unpack(ld_vec(L.q + i), x);
             id0 = L.qid[i];
-            if (a.penalty) hs_penalize<VEC>(L.hs, id0, x, a.rep);
+            if (a.penalty) hs_penalize<VEC>(L.hs, id0, x);
 #pragma unroll
             for (int j = 0; j < VEC; ++j) lm = fmaxf(lm, x[j]);
         }
@@ -450,7 +465,7 @@ __device__ __noinline__ uint64_t greedy_take(const SampleArgs &a, uint32_t id0, 
         float x[VEC];
 #pragma unroll
         for (int j = 0; j < VEC; ++j) x[j] = b.v[u * VEC + j];
-        hs_penalize<VEC>(L.hs, v0, x, a.rep);
+        hs_penalize<VEC>(L.hs, v0, x);
 #pragma unroll
         for (int j = 0; j < VEC; ++j)
             if (x[j] > gx || (x[j] == gx && v0 + j < gid)) {
@@ -467,11 +482,11 @@ __device__ __noinline__ uint64_t greedy_take(const SampleArgs &a, uint32_t id0, 
  * next 9 inside the chosen bin) of the larger elements, whose bin holding the
  * K'-th largest gives the row's starting threshold.  Returns the warp's own
  * threshold. */
-template <typename T>
+template <typename T, int UX>
 __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, int head, int v0, int v1) {
     using F = Fmt<T>;
     constexpr int NT = kRowThreads, NW = kRowWarps;
-    constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U, NE = U * VEC;
+    constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U * UX, NE = U * VEC;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const RowLayout L = row_layout<kTopK>(a, warp);
     float xw[NE];
@@ -480,7 +495,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         const int vi = v0 + u * 32 + lane;
         if (vi < v1) {
             F::unpack(ld_vec(L.q + u * 32 + lane), xw + u * VEC);
-            if (a.penalty) hs_penalize<VEC>(L.hs, (uint32_t)(head + vi * VEC), xw + u * VEC, a.rep);
+            if (a.penalty) hs_penalize<VEC>(L.hs, (uint32_t)(head + vi * VEC), xw + u * VEC);
         } else {
 #pragma unroll
             for (int j = 0; j < VEC; ++j) xw[u * VEC + j] = -INFINITY;
@@ -790,19 +805,22 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
 
 /* Greedy fits 8 CTAs per SM at 64 registers; the queued modes get 72 (7 per
  * SM, still one wave for 1024 rows), which removes most of their spills. */
-template <int MODE>
+template <int MODE, int UX>
 struct RowOcc {
-    static constexpr int kCtas = MODE == kGreedy ? 8 : 7;
+    static constexpr int kCtas = UX > 1 ? 2 : (MODE == kGreedy ? 8 : 7);
 };
 
-template <typename T, int MODE>
-__global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
+/* UX = 1: batches of 16 elements per lane, 7-8 CTAs per SM (a batch that
+ * fills the GPU).  UX = 4: batches four times as wide at 2 CTAs per SM, for
+ * batches too small to fill the GPU: one row's loads in flight grow fourfold,
+ * and a row streams at about four times the rate. */
+template <typename T, int MODE, int UX>
+__global__ void __launch_bounds__(kRowThreads, (RowOcc<MODE, UX>::kCtas))
     sample_rows_kernel(const __grid_constant__ SampleArgs a) {
-    if (a.gate && *a.gate == 0) return;
     using F = Fmt<T>;
     constexpr int NT = kRowThreads, NW = kRowWarps;
-    constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U, NE = U * VEC;
-    static_assert(NE == kLaneElems, "sixteen elements per lane and batch");
+    constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U * UX, NE = U * VEC;
+    static_assert(MODE != kGreedy || NE == kLaneElems, "greedy: sixteen elements per lane and batch");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int row = blockIdx.x;
     const RowSpan span = row_span(a, row);
@@ -827,7 +845,9 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
             rs.l0nan = x0 != x0;  // a NaN at id 0 (the penalty keeps it NaN)
             rs.next = NW;
         }
-        if (a.penalty) hs_build<NT>(L.hs, a.hist + (size_t)span.hrow * a.hld, a.hist_start, a.hist_len, V, span.id_off);
+        if (a.penalty)
+            hs_build<T, NT>(L.hs, a.hist + (size_t)span.hrow * a.hld, a.hist_start, a.hist_len, V, span.id_off, rowp,
+                            a.rep);
         __syncthreads();
     }
 
@@ -861,8 +881,8 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
             ids = scalar_id(g, lane);
             xs = F::scalar(rowp, ids);
             if (a.penalty) {
-                const uint32_t c = hs_count(L.hs, (uint32_t)ids);
-                if (c) xs = apply_penalty(xs, c, a.rep);
+                float v;
+                if (hs_find(L.hs, (uint32_t)ids, v)) xs = v;
             }
         }
         if (MODE == kGreedy) {
@@ -900,12 +920,12 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
     unsigned long long tau_w = 0ull;
     if (MODE == kTopK && min(g.nvec, NW * 32 * U) * VEC >= 4 * a.kprime) {
         /* the first batch goes through this warp's queue, still empty */
-        V8 *const q = reinterpret_cast<V8 *>(row_smem) + warp * kQueueCap;
+        V8 *const q = reinterpret_cast<V8 *>(row_smem) + warp * a.qcap;
 #pragma unroll
         for (int u = 0; u < U; ++u)
             if (v0 + u * 32 + lane < v1) st_vec(q + u * 32 + lane, nxt[u]);
         __syncwarp();
-        tau_w = row_warmup<T>(a, g.head, v0, v1);
+        tau_w = row_warmup<T, UX>(a, g.head, v0, v1);
     }
 
     /* ---- the warp's slice of the vector body ---- */
@@ -966,8 +986,8 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
          * take batches as they free up, so a warp that drained more does
          * not hold up the row end.  28 warps per SM keep enough loads in
          * flight without a register prefetch. */
-        V8 *const wq = reinterpret_cast<V8 *>(row_smem) + warp * kQueueCap;
-        uint32_t *const wqid = reinterpret_cast<uint32_t *>(row_smem + NW * kQueueCap * sizeof(V8)) + warp * kQueueCap;
+        V8 *const wq = reinterpret_cast<V8 *>(row_smem) + warp * a.qcap;
+        uint32_t *const wqid = reinterpret_cast<uint32_t *>(row_smem + NW * a.qcap * sizeof(V8)) + warp * a.qcap;
         int qfill = 0;  // warp-uniform
         auto take = [&]() -> int {  // the next ticket's batch, nbat when none is left
             for (;;) {
@@ -1017,7 +1037,7 @@ __global__ void __launch_bounds__(kRowThreads, RowOcc<MODE>::kCtas)
                     nq += __popc(bal[u]);
                 }
                 if (nq) {
-                    if (qfill + nq > kQueueCap) break;  // drain, then redo this batch
+                    if (qfill + nq > a.qcap) break;  // drain, then redo this batch (qcap >= 32U)
                     const uint32_t id0 = (uint32_t)(g.head + (base + lane) * VEC);
 #pragma unroll
                     for (int u = 0; u < U; ++u) {

@@ -101,6 +101,21 @@ def test_workloads_full_vocab_gpu(cuda, oracle, case):
     assert_parity(name, g, o)
 
 
+@pytest.mark.parametrize("name", ["batch1024", "greedy_penalty", "nucleus_bf16"])
+def test_workloads_full_occupancy_gpu(cuda, oracle, name):
+    """Batches of up to two rows per SM (48 above) run the single-pass kernel
+    with wide batches at 2 CTAs per SM; 560 rows run it at 7-8 CTAs per SM,
+    the path of the full-size workloads."""
+    from noel_b200.workloads import WORKLOADS, generate_numpy
+
+    w = WORKLOADS[name].resized(batch=560)
+    d = generate_numpy(w, seed=13)
+    cfgkw = w.config_kwargs()
+    o = oracle.sample_batch(orc_config(**cfgkw), d["logits"], history=d["history"], rng=d["rng"], n_list=64)
+    g = run_gpu(cuda, cfgkw, d["logits"], d["history"], d["rng"])
+    assert_parity(f"{name}/560", g, o)
+
+
 @pytest.mark.parametrize("pad", [1, 3, 7])
 def test_unaligned_rows_gpu(cuda, oracle, pad):
     """Row stride ld = V + pad puts every row at a different alignment."""

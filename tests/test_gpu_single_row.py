@@ -1,6 +1,6 @@
-"""noel_sampler_sample (the reference's single-row ABI) on rows long enough to
-be split over many CTAs and merged: ids, RNG states, the drawn-from list left
-in candidates, and the penalised entries written back into the caller's host
+"""noel_sampler_sample (the reference's single-row ABI) on full-vocabulary
+rows, three steps each: ids, RNG states, the drawn-from list left in
+candidates, and the penalised entries written back into the caller's host
 row, against the oracle and the reference's in-place penalty
 (sampler.c:87-103)."""
 import numpy as np
@@ -52,7 +52,7 @@ def rows():
 
 
 @pytest.mark.parametrize("case", rows(), ids=lambda c: c[0])
-def test_single_row_split_matches_oracle_gpu(cuda, oracle, case):
+def test_single_row_matches_oracle_gpu(cuda, oracle, case):
     from noel_b200 import sampler as S
 
     name, cfgkw, x0, hist = case
