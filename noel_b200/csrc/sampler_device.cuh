@@ -282,10 +282,15 @@ __device__ void build_history(const HistView &h, const int32_t *hrow, int first,
     if (threadIdx.x == 0) h.gpre[G] = (uint32_t)total;
     for (int i = threadIdx.x; i < total; i += NT) h.cnt[i] = 0u;
     __syncthreads();
-    for (int i = first + threadIdx.x; i < H; i += NT) {
-        const int g = hrow[i];
-        if (g < id_off || g - id_off >= V) continue;
-        atomicAdd(&h.cnt[hist_rank(h, g - id_off)], 1u);
+    for (int b = first; b < H; b += NT) {  // whole warps per round
+        const int i = b + (int)threadIdx.x;
+        const int g = i < H ? hrow[i] : -1;
+        const bool in = i < H && g >= id_off && g - id_off < V;
+        const uint32_t same = __match_any_sync(0xFFFFFFFFu, in ? (uint32_t)(g - id_off) : 0xFFFFFFFFu);
+        /* lanes holding the same id count it once (a skewed window repeats a
+         * few ids in most lanes) */
+        if (in && (int)(threadIdx.x & 31) == __ffs(same) - 1)
+            atomicAdd(&h.cnt[hist_rank(h, g - id_off)], (uint32_t)__popc(same));
     }
     __syncthreads();
 }

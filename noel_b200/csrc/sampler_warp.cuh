@@ -70,16 +70,22 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
     }
     __syncthreads();
     const int bits = __ffs(h.cap) - 1;
-    for (int i = first + threadIdx.x; i < H; i += NT) {
-        const int gt = hrow[i];
-        if (gt < id_off || gt - id_off >= V) continue;  // sampler.c:95 (ids of this shard)
-        const int t = gt - id_off;
+    const int lane = threadIdx.x & 31;
+    for (int base = first; base < H; base += NT) {  // whole warps per round
+        const int i = base + (int)threadIdx.x;
+        const int gt = i < H ? hrow[i] : -1;
+        const bool in = i < H && gt >= id_off && gt - id_off < V;  // sampler.c:95 (ids of this shard)
+        const uint32_t t = in ? (uint32_t)(gt - id_off) : 0xFFFFFFFFu;
+        /* lanes holding the same id insert it once, with their number (a
+         * skewed window repeats a few ids in most lanes) */
+        const uint32_t same = __match_any_sync(kFull, t);
+        if (!in || lane != __ffs(same) - 1) continue;
         atomicOr(&h.blk[t >> 8], 1u << ((t >> 3) & 31));
-        uint32_t p = bits ? (hs_hash((uint32_t)t) >> (32 - bits)) : 0u;
+        uint32_t p = bits ? (hs_hash(t) >> (32 - bits)) : 0u;
         for (int probe = 0; probe < h.cap; ++probe) {
-            const uint32_t prev = atomicCAS(&h.key[p], 0u, (uint32_t)t + 1u);
-            if (prev == 0u || prev == (uint32_t)t + 1u) {
-                atomicAdd(&h.val[p], 1u);
+            const uint32_t prev = atomicCAS(&h.key[p], 0u, t + 1u);
+            if (prev == 0u || prev == t + 1u) {
+                atomicAdd(&h.val[p], (uint32_t)__popc(same));
                 break;
             }
             p = (p + 1) & (uint32_t)(h.cap - 1);
@@ -477,11 +483,14 @@ __device__ __noinline__ uint64_t greedy_take(const SampleArgs &a, uint32_t id0, 
 }
 
 /* Block warm-up on every warp's first batch (all threads of the block): the
- * smallest lane maximum of a warp has 32 of the warp's elements above it; the
- * second largest of those bounds a two-level histogram (9 key bits, then the
- * next 9 inside the chosen bin) of the larger elements, whose bin holding the
- * K'-th largest gives the row's starting threshold.  Returns the warp's own
- * threshold. */
+ * smallest raw lane maximum of a warp has 32 of the warp's raw elements above
+ * it and becomes the warp's own threshold (an exclusion threshold checked at
+ * the row end, so it needs no proof); the second largest of those bounds a
+ * two-level histogram (9 key bits, then the next 9 inside the chosen bin) of
+ * the larger elements, penalised, whose bin holding the K'-th largest gives
+ * the row's starting threshold.  The penalty only lowers values, so only
+ * elements whose raw value reaches the histogram are looked up.  Returns the
+ * warp's own threshold. */
 template <typename T, int UX>
 __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, int head, int v0, int v1) {
     using F = Fmt<T>;
@@ -495,7 +504,6 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         const int vi = v0 + u * 32 + lane;
         if (vi < v1) {
             F::unpack(ld_vec(L.q + u * 32 + lane), xw + u * VEC);
-            if (a.penalty) hs_penalize<VEC>(L.hs, (uint32_t)(head + vi * VEC), xw + u * VEC);
         } else {
 #pragma unroll
             for (int j = 0; j < VEC; ++j) xw[u * VEC + j] = -INFINITY;
@@ -507,7 +515,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
     for (int e = 0; e < NE; ++e) lmax = fmaxf(lmax, xw[e]);  // NaN-ignoring
     const float t0 = warp_min_f(lmax);
     if (t0 > -INFINITY) {
-        tau_w = (unsigned long long)ord_key(t0) << 32;  // 32 of this warp's elements beat it
+        tau_w = (unsigned long long)ord_key(t0) << 32;  // 32 of this warp's raw elements beat it
         if (lane == 0) rs.taus[warp] = tau_w;
     }
     __syncthreads();
@@ -523,6 +531,18 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         }
     }
     const uint32_t lo_key = (uint32_t)(t2 >> 32);
+    if (a.penalty) {  // only what reaches the histogram needs its penalised value
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint32_t id0 = (uint32_t)(head + (v0 + u * 32 + lane) * VEC);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) {
+                float &xv = xw[u * VEC + j];
+                float pv;
+                if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key && hs_find(L.hs, id0 + (uint32_t)j, pv)) xv = pv;
+            }
+        }
+    }
 #pragma unroll
     for (int e = 0; e < NE; ++e) {
         const float xv = xw[e];

@@ -116,6 +116,31 @@ def test_workloads_full_occupancy_gpu(cuda, oracle, name):
     assert_parity(f"{name}/560", g, o)
 
 
+@pytest.mark.parametrize("top_k,T", [(500, 0.9), (40, 0.8), (1, 0.0), (0, 1.0)])
+def test_heavy_penalty_gpu(cuda, oracle, top_k, T):
+    """Histories that repeat the row's largest ids ten times or more (each
+    occurrence divides again, sampler.c:96-100), so the penalty moves most of
+    the row's top entries below the rest: greedy, top-k in the single-pass and
+    block kernels, and the full list."""
+    from noel_b200.workloads import row_states
+
+    g = np.random.Generator(np.random.PCG64(31))
+    B, V = 6, 30000
+    logits = (2.0 * g.standard_normal((B, V))).astype(np.float32)
+    hist = np.zeros((B, 3900), np.int32)
+    for b in range(B):
+        top = np.argsort(-logits[b])[:1200]
+        hist[b] = np.concatenate([np.repeat(top[:300], 10), top[300:1200]])
+        g.shuffle(hist[b])
+    logits[:, 0] = np.abs(logits[:, 0]) + 30.0  # id 0: large raw value, in every window 10 times
+    hist[:, :10] = 0
+    cfgkw = dict(temperature=T, top_p=0.95, top_k=top_k, repetition_penalty=3.0, repetition_window=0, seed=0)
+    rng = row_states(17, np.arange(B))
+    o = oracle.sample_batch(orc_config(**cfgkw), logits, history=hist, rng=rng, n_list=64)
+    r = run_gpu(cuda, cfgkw, logits, hist, rng)
+    assert_parity(f"heavy_penalty k={top_k} T={T}", r, o)
+
+
 @pytest.mark.parametrize("pad", [1, 3, 7])
 def test_unaligned_rows_gpu(cuda, oracle, pad):
     """Row stride ld = V + pad puts every row at a different alignment."""
