@@ -343,7 +343,9 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
             wide = B <= 2 * c->sms;
             const int u = (dtype == NOEL_DTYPE_F32 ? 2 : 1) * (wide ? 4 : 1);  // vectors per lane and batch
             a.qcap = 32 * u > kQueueCap ? 32 * u : kQueueCap;
-            a.ucap = mode == kTopK ? nw * a.kw : nw * a.cap;
+            /* the row-end union: every warp's whole buffer for K' > 32, each
+             * warp's best kw below */
+            a.ucap = mode == kTopK && a.kprime <= 32 ? nw * a.kw : nw * a.cap;
             const size_t gather = (size_t)a.ucap * 8 + (size_t)pow2_at_least(a.ucap) * 8;
             const size_t warm = mode == kTopK ? (size_t)2 * kWarpBins * 4 : 0;
             smem_main += (size_t)nw * a.qcap * (sizeof(V8) + 4) + (size_t)nw * a.cap * 8 +

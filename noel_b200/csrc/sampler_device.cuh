@@ -232,6 +232,26 @@ __device__ void bitonic_sort_desc(uint64_t *a, int P) {
     }
 }
 
+/* Descending bitonic sort of P (a power of two) keys in shared memory by a
+ * whole block, each thread taking pairs (i, i + j) rather than indices, so no
+ * thread idles in a step; ends with a barrier. */
+template <int NT>
+__device__ __forceinline__ void block_bitonic_pairs_desc(uint64_t *a, int P) {
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int p = threadIdx.x; p < (P >> 1); p += NT) {
+                const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1));  // lower index of pair p at distance j
+                const uint64_t ai = a[i], aj = a[i + j];
+                if ((i & k) == 0 ? (ai < aj) : (ai > aj)) {
+                    a[i] = aj;
+                    a[i + j] = ai;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
 /* ---------------------------------------------------------------------- */
 /* history: bitmap of ids in the window, rank -> occurrence count           */
 

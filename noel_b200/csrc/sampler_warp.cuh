@@ -632,6 +632,10 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
         return;
     }
     const float Mfull = rs.l0nan ? __uint_as_float(0x7FC00000u) : key_float(rs.maxkey);
+    /* K' > 32: the whole block sorts the union of the warps' buffers; small
+     * K': each warp brings its best kw and warp 0 selects from their union
+     * (a sort of up to NW buffers costs more than those small selections) */
+    const bool bsort = MODE == kTopK && a.kprime > 32;
     if (MODE == kTopK) {
         /* entries below the shared filter cannot make the top K' */
         const unsigned long long t2 = rs.tsh;
@@ -654,7 +658,7 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
             }
             wcount = wn;
         }
-        if (wcount > kw) {  // each warp brings its best kw to the gather
+        if (!bsort && wcount > kw) {
             tau_w = warp_topk_sorted_r<4>(L.wkey, L.wid, wcount, kw, nullptr, 1);
             wcount = kw;
             wtrunc = true;
@@ -677,9 +681,25 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
         if (tid == 0) list_exact_row(a, row);
         return;
     }
-    for (int i = lane; i < wcount; i += 32) {
-        L.ukey[off + i] = L.wkey[i];
-        L.uid[off + i] = L.wid[i];
+    if (bsort) {
+        /* the union (at most NW buffers) as composite keys, sorted by the
+         * whole block; its best min(nu, K') go to ukey / uid in order */
+        int P = 2;
+        while (P < nu) P <<= 1;
+        for (int i = lane; i < wcount; i += 32) L.sk[off + i] = comp_key(L.wkey[i], L.wid[i]);
+        for (int i = nu + tid; i < P; i += NT) L.sk[i] = 0ull;
+        __syncthreads();
+        block_bitonic_pairs_desc<NT>(L.sk, P);
+        for (int i = tid; i < min(nu, a.kprime); i += NT) {
+            const uint64_t k = L.sk[i];
+            L.ukey[i] = (uint32_t)(k >> 32);
+            L.uid[i] = 0xFFFFFFFFu - (uint32_t)k;
+        }
+    } else {
+        for (int i = lane; i < wcount; i += 32) {
+            L.ukey[off + i] = L.wkey[i];
+            L.uid[off + i] = L.wid[i];
+        }
     }
     __syncthreads();
     if (warp != 0) return;
@@ -694,10 +714,9 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
          * kept key beats that warp's final threshold. */
         unsigned long long worst = 0ull;
         for (int w = 0; w < NW; ++w) worst = max(worst, rs.taus[w]);
-        const unsigned long long T =
-            n < a.kprime ? 0ull
-                         : (a.kprime < 128 ? warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1)
-                                           : warp_topk_sorted_r<8>(L.ukey, L.uid, n, a.kprime, nullptr, 1));
+        const unsigned long long T = n < a.kprime ? 0ull
+                                     : bsort ? (unsigned long long)L.sk[a.kprime - 1]
+                                             : warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
         if (n < a.kprime || T < worst) {  // a warp's cut excludes only keys strictly below it
             if (lane == 0) list_exact_row(a, row);
             return;
@@ -709,10 +728,7 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
     if (MODE == kTopK && a.shard_entries) {
         /* vocab shard: its K' best by (logit desc, id asc), its largest
          * penalised logit, and whether it holds more elements than listed */
-        if (!trunc) {
-            if (a.kprime < 128) warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
-            else warp_topk_sorted_r<8>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
-        }
+        if (!trunc && !bsort) warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
         const int m = min(n, a.kprime);
         const int id_off = row_span(a, row).id_off;
         uint2 *out = a.shard_entries + (size_t)row * a.kprime;
