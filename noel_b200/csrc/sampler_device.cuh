@@ -619,6 +619,67 @@ __device__ __forceinline__ TailOut run_tail(int num_cands, bool more_than_listed
     return o;
 }
 
+/* First i < n with P[i] >= t (P non-decreasing), else n - 1; the whole warp. */
+__device__ __forceinline__ int warp_first_at_least(const float *P, int n, float t) {
+    const int lane = threadIdx.x & 31;
+    for (int b = 0; b < n; b += 32) {
+        const int i = b + lane;
+        const unsigned hit = __ballot_sync(0xFFFFFFFFu, i < n && P[i] >= t);
+        if (hit) return b + __ffs(hit) - 1;
+    }
+    return n - 1;
+}
+
+/* run_tail for a whole warp.  The mass, nucleus and draw loops of
+ * sampler.c:160-191 all walk the same running sum of the sorted weights, so
+ * lane 0 computes that sum once, in order and with the same roundings, into
+ * P[0, n) (shared memory), and the cut (first running sum >= top_p * mass)
+ * and the draw (first running sum >= r) become warp searches: adding
+ * non-negative weights never lowers a rounded sum, so P is non-decreasing.
+ * rng is read and advanced by lane 0 only; every lane gets the result. */
+template <typename WeightAt>
+__device__ __forceinline__ TailOut warp_tail(int num_cands, bool more_than_listed, int top_k, float top_p,
+                                             uint64_t *rng, WeightAt w, float *P) {
+    const int lane = threadIdx.x & 31;
+    TailOut o;
+    int n = num_cands;
+    if (top_k > 0 && (more_than_listed || top_k < n)) n = top_k;  // sampler.c:155-157
+    o.n_topk = n;
+    if (lane == 0) {  // sampler.c:160-163, keeping every partial sum
+        float m = 0.0f;
+        int i = 0;
+        for (; i + 8 <= n; i += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = w(i + j);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                m = __fadd_rn(m, v[j]);
+                P[i + j] = m;
+            }
+        }
+        for (; i < n; ++i) {
+            m = __fadd_rn(m, w(i));
+            P[i] = m;
+        }
+    }
+    __syncwarp();
+    float mass = n > 0 ? P[n - 1] : 0.0f;
+    if (top_p > 0.0f && top_p < 1.0f && n > 0) {  // sampler.c:165-179
+        const int keep = warp_first_at_least(P, n, __fmul_rn(top_p, mass)) + 1;
+        n = keep;
+        mass = P[keep - 1];
+    }
+    o.n_final = n;
+    o.mass = mass;
+    float r = 0.0f;  // sampler.c:182-191
+    if (lane == 0) r = __fmul_rn(rng_uniform(rng), mass);
+    r = __shfl_sync(0xFFFFFFFFu, r, 0);
+    o.pos = n > 0 ? warp_first_at_least(P, n, r) : -1;
+    __syncwarp();
+    return o;
+}
+
 }  // namespace noel
 
 namespace noel {

@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
     const int ncand = block_sum_int<NT>(mine, s_w);  // its barriers publish sk
     bitonic_sort_desc<NT>(sk, P);
 
-    if (tid == 0) {
+    if (tid < 32) {  // warp 0
         bool more = false;
         bool exact = true;
         if (MODE == kTopK && trunc && ncand == n) {
@@ -473,28 +473,37 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
             if (!(v_last < v_k)) exact = false;
         }
         if (!exact) {
-            list_exact_row(a, row);
-            s_fin_n = -1;
+            if (tid == 0) {
+                list_exact_row(a, row);
+                s_fin_n = -1;
+            }
         } else {
             const bool fb = ncand == 0;
-            uint64_t st[2] = {a.rng[2 * (size_t)row], a.rng[2 * (size_t)row + 1]};
+            uint64_t st[2] = {0ull, 0ull};
+            if (tid == 0) {
+                st[0] = a.rng[2 * (size_t)row];
+                st[1] = a.rng[2 * (size_t)row + 1];
+            }
             auto w = [&](int i) -> float {
                 return fb ? 1.0f : __uint_as_float((uint32_t)(sk[i] >> 32));
             };
-            const TailOut t = run_tail(fb ? 1 : ncand, more, a.top_k, a.top_p, st, w);
-            a.rng[2 * (size_t)row] = st[0];
-            a.rng[2 * (size_t)row + 1] = st[1];
-            RowOut o;
-            o.id = fb ? 0 : (int)(0xFFFFFFFFu - (uint32_t)sk[t.pos]);
-            o.prob = __fdiv_rn(w(t.pos), t.mass);
-            o.mass = t.mass;
-            o.n_topk = t.n_topk;
-            o.n_final = t.n_final;
-            o.num_cands = more ? -1 : (fb ? 1 : ncand);
-            o.flags = fb ? NOEL_ROW_FALLBACK : 0;
-            write_row_stats(a, row, o);
-            s_fin_n = fb ? -2 : t.n_final;
-            s_fin_mass = t.mass;
+            /* the running sums go to the warm-up bins (2048 floats >= K') */
+            const TailOut t = warp_tail(fb ? 1 : ncand, more, a.top_k, a.top_p, st, w, reinterpret_cast<float *>(whist));
+            if (tid == 0) {
+                a.rng[2 * (size_t)row] = st[0];
+                a.rng[2 * (size_t)row + 1] = st[1];
+                RowOut o;
+                o.id = fb ? 0 : (int)(0xFFFFFFFFu - (uint32_t)sk[t.pos]);
+                o.prob = __fdiv_rn(w(t.pos), t.mass);
+                o.mass = t.mass;
+                o.n_topk = t.n_topk;
+                o.n_final = t.n_final;
+                o.num_cands = more ? -1 : (fb ? 1 : ncand);
+                o.flags = fb ? NOEL_ROW_FALLBACK : 0;
+                write_row_stats(a, row, o);
+                s_fin_n = fb ? -2 : t.n_final;
+                s_fin_mass = t.mass;
+            }
         }
     }
     __syncthreads();

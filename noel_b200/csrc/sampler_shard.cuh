@@ -173,10 +173,15 @@ __global__ void __launch_bounds__(32 * kMergeWarps) shard_merge_kernel(const __g
     const bool fb = ncand == 0;  // sampler.c:145-149
     int nfin = 0;
     float mass = 0.0f;
+    uint64_t st[2] = {0ull, 0ull};
     if (lane == 0) {
-        uint64_t st[2] = {a.rng[2 * (size_t)row], a.rng[2 * (size_t)row + 1]};
-        auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float((uint32_t)(sk[i] >> 32)); };
-        const TailOut t = run_tail(fb ? 1 : ncand, more_c, a.top_k, a.top_p, st, w);
+        st[0] = a.rng[2 * (size_t)row];
+        st[1] = a.rng[2 * (size_t)row + 1];
+    }
+    auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float((uint32_t)(sk[i] >> 32)); };
+    /* the running sums go where the gathered keys were (no longer read) */
+    const TailOut t = warp_tail(fb ? 1 : ncand, more_c, a.top_k, a.top_p, st, w, reinterpret_cast<float *>(ukey));
+    if (lane == 0) {
         a.rng[2 * (size_t)row] = st[0];
         a.rng[2 * (size_t)row + 1] = st[1];
         a.ids[row] = fb ? 0 : (int)(0xFFFFFFFFu - (uint32_t)sk[t.pos]);

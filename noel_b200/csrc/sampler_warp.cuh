@@ -799,10 +799,15 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
     const bool fb = ncand == 0;
     int nfin = 0;
     float mass = 0.0f;
+    uint64_t st[2] = {0ull, 0ull};
     if (lane == 0) {
-        uint64_t st[2] = {a.rng[2 * (size_t)row], a.rng[2 * (size_t)row + 1]};
-        auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float((uint32_t)(L.sk[i] >> 32)); };
-        const TailOut t = run_tail(fb ? 1 : ncand, more, a.top_k, a.top_p, st, w);
+        st[0] = a.rng[2 * (size_t)row];
+        st[1] = a.rng[2 * (size_t)row + 1];
+    }
+    auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float((uint32_t)(L.sk[i] >> 32)); };
+    /* the running sums go where the gathered keys were (no longer read) */
+    const TailOut t = warp_tail(fb ? 1 : ncand, more, a.top_k, a.top_p, st, w, reinterpret_cast<float *>(L.ukey));
+    if (lane == 0) {
         a.rng[2 * (size_t)row] = st[0];
         a.rng[2 * (size_t)row + 1] = st[1];
         RowOut o;
