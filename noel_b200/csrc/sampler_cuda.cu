@@ -325,7 +325,10 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     size_t smem_main;
     bool wide = false;
     if (block_kernel) {
-        smem_main = hist_bytes + (size_t)a.cap * 8 + kWarmBins * 4;
+        /* the block kernel's history also holds the id of each rank while
+         * it computes the penalised values */
+        const size_t idr = a.penalty ? (size_t)(H - a.hist_start > 1 ? H - a.hist_start : 1) * 4 : 0;
+        smem_main = ((hist_bytes + idr + 15) & ~size_t(15)) + (size_t)a.cap * 8 + kWarmBins * 4;
     } else {
         /* single-pass kernel: bitmap of 8-id blocks + (id, count) table of the window,
          * per-warp buffers, and one area reused by the warm-up histogram and

@@ -258,8 +258,10 @@ __device__ __forceinline__ void block_bitonic_pairs_desc(uint64_t *a, int P) {
 struct HistView {
     uint32_t *bm;    // ceil(V/32) words
     uint32_t *gpre;  // set bits before each 8-word group; [G] = total
-    uint32_t *cnt;   // occurrences per distinct id, indexed by rank
+    uint32_t *cnt;   // per distinct id, indexed by rank: occurrences, or (with
+                     // idr) the penalised logit as float bits once built
     int words;
+    uint32_t *idr;   // optional scratch: id of each rank while building
 };
 
 __device__ __forceinline__ int hist_rank(const HistView &h, int t) {
@@ -269,18 +271,27 @@ __device__ __forceinline__ int hist_rank(const HistView &h, int t) {
     return r + __popc(h.bm[w] & ((1u << (t & 31)) - 1u));
 }
 
-/* sampler.c:88-93: the window of the row's history, ids in [0, V) only */
-template <int NT>
+/* sampler.c:88-93: the window of the row's history, ids in [0, V) only.
+ * Lanes of a warp whose ids share a bitmap word set it with one atomic, and
+ * lanes holding the same id count it once (a skewed window repeats a few low
+ * ids in most lanes).  With h.idr, every distinct id's count then becomes its
+ * penalised logit (sampler.c:96-100, once per occurrence), computed once per
+ * row with the ranks spread over the threads. */
+template <int NT, typename T = float>
 __device__ void build_history(const HistView &h, const int32_t *hrow, int first, int H, int V,
-                              int *s_w, int id_off = 0) {
+                              int *s_w, int id_off = 0, const void *rowp = nullptr, float rep = 1.0f) {
     const int W = h.words, G = (W + 7) >> 3;
     for (int i = threadIdx.x; i < W; i += NT) h.bm[i] = 0u;
     __syncthreads();
-    for (int i = first + threadIdx.x; i < H; i += NT) {
-        const int g = hrow[i];
-        if (g < id_off || g - id_off >= V) continue;  // sampler.c:95 (ids of this shard)
+    for (int b = first; b < H; b += NT) {  // whole warps per round
+        const int i = b + (int)threadIdx.x;
+        const int g = i < H ? hrow[i] : -1;
+        const bool in = i < H && g >= id_off && g - id_off < V;  // sampler.c:95 (ids of this shard)
         const int t = g - id_off;
-        atomicOr(&h.bm[t >> 5], 1u << (t & 31));
+        const uint32_t wd = in ? (uint32_t)(t >> 5) : 0xFFFFFFFFu;
+        const uint32_t grp = __match_any_sync(0xFFFFFFFFu, wd);
+        const uint32_t bits = __reduce_or_sync(grp, in ? 1u << (t & 31) : 0u);
+        if (in && (int)(threadIdx.x & 31) == __ffs(grp) - 1) atomicOr(&h.bm[wd], bits);
     }
     __syncthreads();
     const int per = (G + NT - 1) / NT;
@@ -309,10 +320,24 @@ __device__ void build_history(const HistView &h, const int32_t *hrow, int first,
         const uint32_t same = __match_any_sync(0xFFFFFFFFu, in ? (uint32_t)(g - id_off) : 0xFFFFFFFFu);
         /* lanes holding the same id count it once (a skewed window repeats a
          * few ids in most lanes) */
-        if (in && (int)(threadIdx.x & 31) == __ffs(same) - 1)
-            atomicAdd(&h.cnt[hist_rank(h, g - id_off)], (uint32_t)__popc(same));
+        if (in && (int)(threadIdx.x & 31) == __ffs(same) - 1) {
+            const int r = hist_rank(h, g - id_off);
+            const uint32_t before = atomicAdd(&h.cnt[r], (uint32_t)__popc(same));
+            if (h.idr && before == 0u) h.idr[r] = (uint32_t)(g - id_off);  // the first count names the rank
+        }
     }
     __syncthreads();
+    if (h.idr) {
+        const int total = (int)h.gpre[G];
+        for (int r = threadIdx.x; r < total; r += NT)
+        {
+            const int id = (int)h.idr[r];
+            const float x = sizeof(T) == 4 ? static_cast<const float *>(rowp)[id]  // fp32, or bf16 widened
+                                           : __uint_as_float((uint32_t)static_cast<const uint16_t *>(rowp)[id] << 16);
+            h.cnt[r] = __float_as_uint(apply_penalty(x, h.cnt[r], rep));
+        }
+        __syncthreads();
+    }
 }
 
 /* penalty bits of ids [id0, id0+n) (n <= 16) */

@@ -39,8 +39,7 @@ __device__ void write_back_penalty(const SampleArgs &a, const HistView &hv, int 
             const int j = __ffs(bits) - 1;
             bits &= bits - 1;
             const int id = w * 32 + j;
-            const uint32_t c = hv.cnt[hist_rank(hv, id)];
-            wrow[id] = apply_penalty(wrow[id], c, a.rep);
+            wrow[id] = __uint_as_float(hv.cnt[hist_rank(hv, id)]);  // penalised value
         }
     }
 }
@@ -85,6 +84,8 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
         sp += (size_t)(G + 1) * 4;
         hv.cnt = reinterpret_cast<uint32_t *>(sp);
         sp += (size_t)max(1, a.hist_len - a.hist_start) * 4;
+        hv.idr = reinterpret_cast<uint32_t *>(sp);
+        sp += (size_t)max(1, a.hist_len - a.hist_start) * 4;
         sp = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(sp) + 15) & ~uintptr_t(15));
     }
     Buf buf{nullptr, nullptr};
@@ -104,7 +105,9 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
         s_tau_id = 0xFFFFFFFFu;
         s_maxkey = kKeyNegInf;
     }
-    if (a.penalty) build_history<NT>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w, a.id_off);
+    if (a.penalty)  // hv.cnt then holds penalised values
+        build_history<NT, T>(hv, a.hist + (size_t)row * a.hld, a.hist_start, a.hist_len, V, s_w, a.id_off, rowp,
+                             a.rep);
     __syncthreads();
 
     const RowGeom g = row_geom<T>(rowp, V);
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
         const int id = scalar_id(g, tid);
         float x = F::scalar(rowp, id);
         if (a.penalty && ((hv.bm[id >> 5] >> (id & 31)) & 1u))
-            x = apply_penalty(x, hv.cnt[hist_rank(hv, id)], a.rep);
+            x = __uint_as_float(hv.cnt[hist_rank(hv, id)]);
         if (id == 0 && x != x) s_l0nan = 1;
         if (MODE == kGreedy) {
             if (x > gx || (x == gx && (uint32_t)id < gid)) {
@@ -185,10 +188,10 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
                     while (bits) {
                         const int j = __ffs(bits) - 1;
                         bits &= bits - 1;
-                        const uint32_t c = hv.cnt[hist_rank(hv, id0 + j)];
+                        const float pv = __uint_as_float(hv.cnt[hist_rank(hv, id0 + j)]);  // penalised value
 #pragma unroll
                         for (int jj = 0; jj < VEC; ++jj)
-                            if (jj == j) x[u * VEC + jj] = apply_penalty(x[u * VEC + jj], c, a.rep);
+                            if (jj == j) x[u * VEC + jj] = pv;
                     }
                 }
             }
@@ -460,7 +463,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
         for (int i = n + tid; i < P; i += NT) sk[i] = 0ull;
     }
     const int ncand = block_sum_int<NT>(mine, s_w);  // its barriers publish sk
-    bitonic_sort_desc<NT>(sk, P);
+    block_bitonic_pairs_desc<NT>(sk, P);
 
     if (tid < 32) {  // warp 0
         bool more = false;
