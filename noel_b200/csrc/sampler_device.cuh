@@ -655,6 +655,84 @@ __device__ __forceinline__ int warp_first_at_least(const float *P, int n, float 
     return n - 1;
 }
 
+/* First i in [0, n) with P[i] >= t for a non-decreasing P in global memory
+ * (whole warp): 32-way narrowing, then one ballot; n - 1 if there is none. */
+__device__ __forceinline__ int warp_search_at_least(const float *P, int n, float t) {
+    const int lane = threadIdx.x & 31;
+    int lo = 0, hi = n;  // the answer, if any, is in [lo, hi)
+    while (hi - lo > 32) {
+        const int step = (hi - lo + 31) / 32;
+        const int idx = lo + lane * step;
+        const unsigned hit = __ballot_sync(0xFFFFFFFFu, idx < hi && P[idx] >= t);
+        if (hit & 1u) return lo;  // P[lo] >= t
+        if (hit) {
+            const int L = __ffs(hit) - 1;  // P[lo + L step] >= t > P[lo + (L - 1) step]
+            hi = lo + L * step + 1;
+            lo = lo + (L - 1) * step + 1;
+        } else {
+            lo += ((hi - 1 - lo) / step) * step + 1;  // past the last sampled index
+        }
+    }
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, lo + lane < hi && P[lo + lane] >= t);
+    return hit ? lo + __ffs(hit) - 1 : n - 1;
+}
+
+/* warp_tail for long lists held in global memory (the two-pass kernel):
+ * the warp stages 256 weights at a time in shared memory (stage), lane 0
+ * adds them in order, the running sums go to P (global, n floats), and the
+ * cut and the draw are 32-way searches over P. */
+template <typename WeightAt>
+__device__ __forceinline__ TailOut warp_tail_global(int num_cands, bool more_than_listed, int top_k, float top_p,
+                                                    uint64_t *rng, WeightAt w, float *P, float *stage) {
+    const int lane = threadIdx.x & 31;
+    TailOut o;
+    int n = num_cands;
+    if (top_k > 0 && (more_than_listed || top_k < n)) n = top_k;  // sampler.c:155-157
+    o.n_topk = n;
+    float m = 0.0f;  // sampler.c:160-163, keeping every partial sum (lane 0's)
+    for (int b = 0; b < n; b += 256) {
+        const int c = min(256, n - b);
+        for (int j = lane; j < c; j += 32) stage[j] = w(b + j);
+        __syncwarp();
+        if (lane == 0) {
+            int j = 0;
+            for (; j + 8 <= c; j += 8) {
+                float v[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v[q] = stage[j + q];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    m = __fadd_rn(m, v[q]);
+                    stage[j + q] = m;
+                }
+            }
+            for (; j < c; ++j) {
+                m = __fadd_rn(m, stage[j]);
+                stage[j] = m;
+            }
+        }
+        __syncwarp();
+        for (int j = lane; j < c; j += 32) P[b + j] = stage[j];
+        __syncwarp();
+    }
+    __threadfence_block();
+    __syncwarp();
+    float mass = __shfl_sync(0xFFFFFFFFu, m, 0);
+    if (top_p > 0.0f && top_p < 1.0f && n > 0) {  // sampler.c:165-179
+        const int keep = warp_search_at_least(P, n, __fmul_rn(top_p, mass)) + 1;
+        n = keep;
+        mass = P[keep - 1];
+    }
+    o.n_final = n;
+    o.mass = mass;
+    float r = 0.0f;  // sampler.c:182-191
+    if (lane == 0) r = __fmul_rn(rng_uniform(rng), mass);
+    r = __shfl_sync(0xFFFFFFFFu, r, 0);
+    o.pos = n > 0 ? warp_search_at_least(P, n, r) : -1;
+    __syncwarp();
+    return o;
+}
+
 /* run_tail for a whole warp.  The mass, nucleus and draw loops of
  * sampler.c:160-191 all walk the same running sum of the sorted weights, so
  * lane 0 computes that sum once, in order and with the same roundings, into

@@ -714,24 +714,32 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
             __syncthreads();
             continue;
         }
-        if (tid == 0) {
-            uint64_t st[2] = {a.rng[2 * (size_t)row], a.rng[2 * (size_t)row + 1]};
+        if (tid < 32) {  // warp 0: running sums into the other slot, staged through s_h
+            uint64_t st[2] = {0ull, 0ull};
+            if (tid == 0) {
+                st[0] = a.rng[2 * (size_t)row];
+                st[1] = a.rng[2 * (size_t)row + 1];
+            }
             auto w = [&](int i) -> float { return fb ? 1.0f : __uint_as_float(~sorted[i].x); };
-            const TailOut t = run_tail(fb ? 1 : n, false, a.top_k, a.top_p, st, w);
-            a.rng[2 * (size_t)row] = st[0];
-            a.rng[2 * (size_t)row + 1] = st[1];
-            RowOut o;
-            o.id = fb ? 0 : (int)sorted[t.pos].y;
-            o.prob = __fdiv_rn(w(t.pos), t.mass);
-            o.mass = t.mass;
-            o.n_topk = t.n_topk;
-            o.n_final = t.n_final;
-            o.num_cands = fb ? 1 : n;
-            o.flags = NOEL_ROW_EXACT_PASS | (fb ? NOEL_ROW_FALLBACK : 0);
-            write_row_stats(a, row, o);
-            s_fin_n = fb ? -2 : t.n_final;
-            s_fin_mass = t.mass;
-            s_sorted = sorted;
+            float *sums = reinterpret_cast<float *>(sorted == slotA ? slotB : slotA);
+            const TailOut t = warp_tail_global(fb ? 1 : n, false, a.top_k, a.top_p, st, w, sums,
+                                               reinterpret_cast<float *>(s_h));
+            if (tid == 0) {
+                a.rng[2 * (size_t)row] = st[0];
+                a.rng[2 * (size_t)row + 1] = st[1];
+                RowOut o;
+                o.id = fb ? 0 : (int)sorted[t.pos].y;
+                o.prob = __fdiv_rn(w(t.pos), t.mass);
+                o.mass = t.mass;
+                o.n_topk = t.n_topk;
+                o.n_final = t.n_final;
+                o.num_cands = fb ? 1 : n;
+                o.flags = NOEL_ROW_EXACT_PASS | (fb ? NOEL_ROW_FALLBACK : 0);
+                write_row_stats(a, row, o);
+                s_fin_n = fb ? -2 : t.n_final;
+                s_fin_mass = t.mass;
+                s_sorted = sorted;
+            }
         }
         __syncthreads();
         if (a.list_ids) {
