@@ -531,22 +531,53 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         }
     }
     const uint32_t lo_key = (uint32_t)(t2 >> 32);
-    if (a.penalty) {  // only what reaches the histogram needs its penalised value
+    /* The elements whose raw value reaches a floor form a bitmask; one
+     * compact loop takes each one's value back from this warp's queue (which
+     * still holds the batch) and its penalised value from the table (the
+     * penalty only lowers values, so the raw test loses nothing).  With wide
+     * batches (64 elements per lane) this saves about 10 us per row over
+     * lookups unrolled across all NE registers; with 16 per lane the unrolled
+     * form is slightly faster and stays. */
+    const V8 *const wq = L.q;
+    auto value = [&](int e) -> float {
+        const int u = e / VEC, j = e - (e / VEC) * VEC;
+        float x = F::scalar(wq + u * 32 + lane, j);
+        float pv;
+        if (a.penalty && hs_find(L.hs, (uint32_t)(head + (v0 + u * 32 + lane) * VEC + j), pv)) x = pv;
+        return x;
+    };
+    auto reach = [&](uint32_t floor_key) -> uint64_t {
+        uint64_t m = 0ull;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const uint32_t id0 = (uint32_t)(head + (v0 + u * 32 + lane) * VEC);
+        for (int e = 0; e < NE; ++e) {
+            const float xv = xw[e];
+            if (xv == xv && xv > -INFINITY && ord_key(xv) >= floor_key) m |= 1ull << e;
+        }
+        return m;
+    };
+    if (UX > 1) {
+        for (uint64_t m = reach(lo_key); m; m &= m - 1) {
+            const float xv = value(__ffsll((long long)m) - 1);
+            if (ord_key(xv) >= lo_key) atomicAdd(&L.area[ord_key(xv) >> 23], 1u);
+        }
+    } else {
+        if (a.penalty) {  // only what reaches the histogram needs its penalised value
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) {
-                float &xv = xw[u * VEC + j];
-                float pv;
-                if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key && hs_find(L.hs, id0 + (uint32_t)j, pv)) xv = pv;
+            for (int u = 0; u < U; ++u) {
+                const uint32_t id0 = (uint32_t)(head + (v0 + u * 32 + lane) * VEC);
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) {
+                    float &xv = xw[u * VEC + j];
+                    float pv;
+                    if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key && hs_find(L.hs, id0 + (uint32_t)j, pv)) xv = pv;
+                }
             }
         }
-    }
 #pragma unroll
-    for (int e = 0; e < NE; ++e) {
-        const float xv = xw[e];
-        if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key) atomicAdd(&L.area[ord_key(xv) >> 23], 1u);
+        for (int e = 0; e < NE; ++e) {
+            const float xv = xw[e];
+            if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key) atomicAdd(&L.area[ord_key(xv) >> 23], 1u);
+        }
     }
     __syncthreads();
     int need;
@@ -555,11 +586,18 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         uint32_t *h2 = L.area + kWarpBins;
         for (int i = tid; i < kWarpBins; i += NT) h2[i] = 0u;
         __syncthreads();
+        if (UX > 1) {
+            for (uint64_t m = reach((uint32_t)wb1 << 23); m; m &= m - 1) {
+                const float xv = value(__ffsll((long long)m) - 1);
+                if (xv == xv && (int)(ord_key(xv) >> 23) == wb1) atomicAdd(&h2[(ord_key(xv) >> 14) & (kWarpBins - 1)], 1u);
+            }
+        } else {
 #pragma unroll
-        for (int e = 0; e < NE; ++e) {
-            const float xv = xw[e];
-            if (xv == xv && xv > -INFINITY && (int)(ord_key(xv) >> 23) == wb1)
-                atomicAdd(&h2[(ord_key(xv) >> 14) & (kWarpBins - 1)], 1u);
+            for (int e = 0; e < NE; ++e) {
+                const float xv = xw[e];
+                if (xv == xv && xv > -INFINITY && (int)(ord_key(xv) >> 23) == wb1)
+                    atomicAdd(&h2[(ord_key(xv) >> 14) & (kWarpBins - 1)], 1u);
+            }
         }
         __syncthreads();
         int need2;
