@@ -38,10 +38,19 @@ sys.path.insert(0, ROOT)
 METRIC = "sampled rows/s at batch 1024×vocab 152064 fp32; % of B200 HBM peak"
 
 
+def workload_of(args):
+    """The named workload, at --batch rows per GPU when given (a smaller case
+    of the same rows for profiler captures; bench lines keep the full size)."""
+    from noel_b200.workloads import WORKLOADS
+
+    w = WORKLOADS[args.workload]
+    return w.resized(batch=args.batch) if args.batch else w
+
+
 def metric_for(w) -> str:
     """The headline metric for the batch1024 workload; other workloads name
     their own shape (they are the other configurations, not the headline)."""
-    if w.name == "batch1024":
+    if w.name == "batch1024" and w.batch == 1024:
         return METRIC
     return f"sampled rows/s, workload {w.name}: batch {w.batch}×vocab {w.vocab} {w.dtype}"
 
@@ -184,7 +193,7 @@ def run_reference(args):
     from noel_b200.workloads import WORKLOADS, generate_numpy
     from oracle.oracle import RefSampler
 
-    w = WORKLOADS[args.workload]
+    w = workload_of(args)
     sample_rows = args.cpu_rows
     d = generate_numpy(w, seed=1, rows=sample_rows)
     threads = RefSampler().max_threads() if RefSampler.available() else os.cpu_count()
@@ -228,7 +237,7 @@ def run_ours(args):
 
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local if world > 1 else 0)
-    w = WORKLOADS[args.workload]
+    w = workload_of(args)
     d = generate_torch(w, dev, seed=1, row0=rank * w.batch)
     logits, hist, rng = d["logits"], d["history"], d["rng"]
     cfg = S.make_config(**w.config_kwargs())
@@ -361,7 +370,7 @@ def run_vocab_sharded(args):
 
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local if world > 1 else 0)
-    w = WORKLOADS[args.workload]
+    w = workload_of(args)
     d = generate_torch(w, dev, seed=1)  # the same full rows on every rank
     b0, width = shard_bounds(w.vocab, world)[rank]
     shard = d["logits"][:, b0:b0 + width].contiguous()
@@ -472,6 +481,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="only W + K steps, for ncu")
+    ap.add_argument("--batch", type=int, default=0, help="rows per GPU instead of the workload's (profiling)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
