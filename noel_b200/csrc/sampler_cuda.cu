@@ -187,7 +187,20 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, size_
     CUDA_TRY(cudaGetLastError());
     if (t_ev_after) CUDA_TRY(cudaEventRecord(t_ev_after, s));
     if (mode != kGreedy) {
-        exact_rows_kernel<T><<<a0.nslots, kExactThreads, smem_exact, s>>>(a0);
+        /* launched as a programmatic dependent of the main kernel: its launch
+         * overlaps the main kernel's last CTAs, and it waits for that grid
+         * (griddepcontrol.wait) before it reads the row list */
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(a0.nslots);
+        lc.blockDim = dim3(kExactThreads);
+        lc.dynamicSmemBytes = smem_exact;
+        lc.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        CUDA_TRY(cudaLaunchKernelEx(&lc, exact_rows_kernel<T>, a0));
         CUDA_TRY(cudaGetLastError());
     }
     return NOEL_OK;

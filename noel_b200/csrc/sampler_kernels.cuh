@@ -606,6 +606,9 @@ __device__ uint2 *radix_sort_stable(uint2 *A, uint2 *B, int n, uint32_t *s_h, in
 
 template <typename T>
 __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleArgs a) {
+    /* launched as a programmatic dependent of the main kernel: wait until
+     * that grid has finished and its writes (the row list) are visible */
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     using F = Fmt<T>;
     constexpr int NT = kExactThreads, NW = NT / 32, IPT = 16;
     extern __shared__ __align__(16) unsigned char smem[];
