@@ -183,6 +183,39 @@ def cpu_reference_rows_per_s(w, logits_host: np.ndarray, hist_host, rng_host, th
     return len(logits_host) / dt, dt
 
 
+def uniform_of(state) -> np.float32:
+    """The reference's next uniform for an xorshift128+ state (sampler.c:8-21)."""
+    a, b = int(state[0]), int(state[1])
+    M = (1 << 64) - 1
+    a ^= (a << 23) & M
+    s1 = a ^ b ^ (a >> 18) ^ (b >> 5)
+    return np.float32((((s1 + b) & M) >> 40)) * np.float32(1.0 / 16777216.0)
+
+
+def boundary_draws(w, cand_vals, num_cands, rng0, rel=1e-5) -> int:
+    """Rows whose draw r lands within rel x mass of a boundary of the running
+    weight sums (sampler.c:155-191, replayed in fp32 on the reference's sorted
+    weights): the draws a tolerance-based comparison would have to excuse."""
+    hits = 0
+    for b in range(len(rng0)):
+        n = int(num_cands[b])
+        if w.top_k > 0 and w.top_k < n:
+            n = w.top_k
+        n = min(n, cand_vals.shape[1])
+        vals = cand_vals[b, :n].astype(np.float32)
+        acc = np.cumsum(vals, dtype=np.float32)  # sequential fp32 sums
+        mass = acc[-1] if n else np.float32(0)
+        if 0.0 < w.top_p < 1.0 and n:
+            keep = int(np.argmax(acc >= np.float32(w.top_p) * mass)) + 1
+            acc, mass = acc[:keep], acc[keep - 1]
+        if not n or mass <= 0:
+            continue
+        r = uniform_of(rng0[b]) * mass
+        if np.min(np.abs(acc - r)) <= rel * mass:
+            hits += 1
+    return hits
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU sampler on the host cores, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
@@ -209,7 +242,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": metric_for(w), "value": value, "unit": "rows/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_label(w),
         "data": "synthetic", "config": workload_config(w, args.gpus),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "reference",
                          "sample": f"{sample_rows} rows of {w.name} per step (one noel_sampler_t per "
@@ -218,6 +251,11 @@ def run_reference(args):
     }
     del torch
     print(json.dumps(line), flush=True)
+
+
+def dtype_label(w) -> str:
+    """The logits' type; the arithmetic is fp32 either way (bf16 widens exactly)."""
+    return "bf16" if w.dtype == "bf16" else "f32"
 
 
 def workload_config(w, n_gpus):
@@ -252,6 +290,7 @@ def run_ours(args):
         S.sample_batch_raw(cfg, logits.data_ptr(), dtype, B, V, logits.stride(0), hp, H, hld,
                            rng.data_ptr(), ids.data_ptr(), probs.data_ptr(), stream.cuda_stream)
 
+    rng0 = rng.clone()  # the states before any step, for the parity check
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -315,18 +354,39 @@ def run_ours(args):
     h2d = lg_np.nbytes + (hist_np.nbytes if hist_np is not None else 0) + rng_np.nbytes
     d2h = B * 4 + rng_np.nbytes
 
-    # ---- CPU baseline: the reference sampler on a bounded sample, rank 0 ----
-    cpu = None
+    # ---- CPU baseline and parity: the reference sampler on a bounded sample
+    # of the same rows from the same initial states, rank 0.  The GPU's ids
+    # and RNG states for those rows (one step from the initial states) must
+    # equal the reference's bit for bit, or the run fails. ----
+    cpu, parity = None, None
     if rank == 0 and not args.no_cpu:
         from oracle.oracle import RefSampler
 
         if RefSampler.available():
             n = min(args.cpu_rows, B)
+            rng_p = rng0.clone()
+            ids_p = torch.empty(B, dtype=torch.int32, device=dev)
+            S.sample_batch_raw(cfg, logits.data_ptr(), dtype, B, V, logits.stride(0), hp, H, hld,
+                               rng_p.data_ptr(), ids_p.data_ptr(), None, stream.cuda_stream)
+            torch.cuda.synchronize()
+            rng0_np = rng0[:n].cpu().numpy().view(np.uint64).copy()
+            lg_ref = lg_np[:n].copy() if dtype == S.F32 else (lg_np[:n].astype(np.uint32) << 16).view(np.float32)
             threads = RefSampler().max_threads()
-            rps, _ = cpu_reference_rows_per_s(w, lg_np[:n].copy() if dtype == S.F32 else
-                                              (lg_np[:n].astype(np.uint32) << 16).view(np.float32),
-                                              hist_np[:n].copy() if hist_np is not None else None,
-                                              rng_np[:n].copy(), threads)
+            ref_cfg = __import__("oracle.oracle", fromlist=["make_config"]).make_config(**w.config_kwargs())
+            t0 = time.perf_counter()
+            ref = RefSampler().sample_batch(ref_cfg, lg_ref, history=hist_np[:n].copy() if hist_np is not None
+                                            else None, rng=rng0_np, n_list=64, nthreads=threads)
+            rps = n / (time.perf_counter() - t0)
+            g_ids = ids_p[:n].cpu().numpy()
+            g_rng = rng_p[:n].cpu().numpy().view(np.uint64)
+            mism = (g_ids != ref.ids) | (g_rng != ref.rng).any(axis=1)
+            parity = {"rows": n, "mismatches": int(mism.sum()),
+                      "boundary_draws": boundary_draws(w, ref.cand_vals, ref.num_cands, rng0_np),
+                      "against": "the reference's src/sampler.c built into oracle/_ref, same rows and states"}
+            if mism.any():
+                print(json.dumps({"error": "parity", "parity": parity,
+                                  "first_rows": np.where(mism)[0][:8].tolist()}), flush=True)
+                sys.exit(1)
             cpu = {"value": rps, "unit": "rows/s", "cores": threads, "kind": "reference",
                    "sample": f"{n} rows of {w.name} (one noel_sampler_t per OpenMP thread)"}
         else:
@@ -337,13 +397,14 @@ def run_ours(args):
         line = {
             "metric": metric_for(w), "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": t_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype_label(w), "data": "synthetic",
             "config": workload_config(w, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "kernel": "sample_rows_kernel", "kernel_ms": k_ms,
                          "bytes_per_launch": bytes_per_launch, "peak_source": f"{peak_kind} hbm_gbs"},
             "cpu_baseline": cpu,
+            "parity": parity,
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "api": "noel_sampler_sample_batch_host (pinned host buffers)"},
             "clocks": clk,

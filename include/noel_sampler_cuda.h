@@ -154,10 +154,21 @@ int noel_sampler_sample_batch_host(const noel_sampler_config_t *cfg, const void 
 /*
  * Wait for the work queued on stream and report device-side failures of the
  * batched calls made on it since the last check: NOEL_ERR_DEVICE_WAIT if a
- * kernel's bounded wait for its row data ran out (the kernel then returns
- * instead of hanging).  Clears the flag.
+ * wait of the streaming kernel (for a ring stage, a prepared row or the
+ * consumers of a row) ran out of its limit; the kernel then returns instead
+ * of hanging and the results of that call are invalid.  Clears the flag.
  */
 int noel_sampler_cuda_sync_check(void *stream);
+
+/*
+ * Limit of every device-side wait of the batched calls this thread makes
+ * next, in nanoseconds of the GPU's global timer (0 restores the default of
+ * 2 s).  stall_next_call = 1 makes the next batched call's kernel issue no
+ * row loads, so its waits run out and noel_sampler_cuda_sync_check reports
+ * NOEL_ERR_DEVICE_WAIT: the failure-detection path, exercised without a GPU
+ * fault.  No counterpart in the reference (its sampler never waits).
+ */
+int noel_sampler_cuda_set_wait_limit(long long wait_ns, int stall_next_call);
 
 /* Calling thread's last status (NOEL_OK after a successful call). */
 int noel_sampler_cuda_last_error(void);

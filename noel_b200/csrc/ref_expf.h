@@ -29,8 +29,10 @@
 
 #if defined(__CUDACC__)
 #define NOEL_HD __host__ __device__ __forceinline__
+#define NOEL_HD_COLD __host__ __device__ __noinline__ /* the rare path: one copy of its code */
 #else
 #define NOEL_HD static inline
+#define NOEL_HD_COLD static
 #endif
 
 /* Domain of the table: float bit patterns [-0.0, -15.0). */
@@ -127,7 +129,7 @@ NOEL_HD noel_dd noel_dd_div_d(noel_dd a, double b) {
  * accurate to well beyond 2^-90 relative.  ln 2 is split as the double
  * nearest to it plus the double nearest to the remainder.
  */
-NOEL_HD noel_dd noel_dd_exp(float xf) {
+NOEL_HD_COLD noel_dd noel_dd_exp(float xf) {
     const noel_dd ln2 = {0.6931471805599453094172321, 2.319046813846299558417771e-17};
     const double x = (double)xf;
     const double k = nearbyint(x * 1.4426950408889634073599247);

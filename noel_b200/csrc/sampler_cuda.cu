@@ -22,7 +22,7 @@
 #include <vector>
 
 #include "noel_sampler_cuda.h"
-#include "sampler_kernels.cuh"
+#include "sampler_stream.cuh"
 
 #define NOEL_EXPF_QUAL static __device__ const
 #include "_gen/expf_table.inc"
@@ -114,8 +114,16 @@ int workspace(DeviceCtx *c, cudaStream_t s, int rows, int vocab, Workspace **out
         *out = &w;
         return NOEL_OK;
     }
+    /* growing synchronises the stream and frees the old buffers, which a
+     * stream being captured into a CUDA graph cannot do: the first call of
+     * each shape on a stream must come before capture */
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone)
+        return fail(NOEL_ERR_UNSUPPORTED,
+                    "the stream is being captured and its scratch must grow: make one call of this shape "
+                    "(%d rows x %d tokens) on the stream before capturing", rows, vocab);
     /* grow to cover both the old and the new shape, so calls that alternate
-     * between shapes (a split row and its whole-row fallback) settle at once */
+     * between shapes settle at once */
     int rc = rows > 1 ? rows : 1, vc = vocab, ns = nslots > 1 ? nslots : 1;
     if (w.counters) {
         rc = rc > w.rows_cap ? rc : w.rows_cap;
@@ -141,6 +149,12 @@ int workspace(DeviceCtx *c, cudaStream_t s, int rows, int vocab, Workspace **out
 /* events recorded around the next main-kernel launches of this thread (profiling hook) */
 thread_local cudaEvent_t t_ev_before = nullptr, t_ev_after = nullptr;
 
+/* limit of the streaming kernel's device-side waits, and the failure-
+ * detection hook (the next call's kernel issues no row loads) */
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
+thread_local unsigned long long t_wait_ns = kDefaultWaitNs;
+thread_local int t_stall_next = 0;
+
 int set_smem(DeviceCtx *c, const void *kernel, size_t bytes) {
     std::lock_guard<std::mutex> lk(g_mu);
     size_t &cur = c->smem_set[kernel];
@@ -158,14 +172,21 @@ int pow2_at_least(int x) {
 }
 
 constexpr int kMaxKprime = 1024;     // top-k mode up to k = 1016
+constexpr size_t kStreamStaticReserve = 4096;  // static shared memory of the streaming kernel, rounded up
+/* modes the persistent streaming kernel serves (the others use the one-CTA-
+ * per-row kernels, measured faster for them so far) */
+constexpr unsigned kStreamModes = 1u << kFullList;
 constexpr int kWarpKprimeMax = 128;  // warp-streaming kernel up to k = 120
 constexpr int kCapMax = 4096;
 
 template <typename T>
-int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, size_t smem_main, size_t smem_exact,
-             DeviceCtx *c, cudaStream_t s) {
+int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, bool stream, size_t smem_main,
+             size_t smem_exact, DeviceCtx *c, cudaStream_t s) {
     const void *kmain = nullptr;
-    if (block_kernel) kmain = (const void *)sample_rows_block_kernel<T, kTopK>;
+    if (stream) kmain = mode == kGreedy ? (const void *)stream_rows_kernel<T, kGreedy>
+                        : mode == kTopK ? (const void *)stream_rows_kernel<T, kTopK>
+                                        : (const void *)stream_rows_kernel<T, kFullList>;
+    else if (block_kernel) kmain = (const void *)sample_rows_block_kernel<T, kTopK>;
     else if (mode == kGreedy) kmain = (const void *)sample_rows_kernel<T, kGreedy, 1>;
     else if (mode == kTopK) kmain = wide ? (const void *)sample_rows_kernel<T, kTopK, 4>
                                          : (const void *)sample_rows_kernel<T, kTopK, 1>;
@@ -177,8 +198,12 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, size_
     r = set_smem(c, kexact, smem_exact);
     if (r) return r;
     if (t_ev_before) CUDA_TRY(cudaEventRecord(t_ev_before, s));
-    const int grid = a0.batch;  // one CTA per row
-    if (block_kernel) sample_rows_block_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
+    const int grid = a0.batch;  // one CTA per row (the streaming kernel: one per SM, rows in turn)
+    const int sgrid = a0.batch < c->sms ? a0.batch : c->sms;
+    if (stream && mode == kGreedy) stream_rows_kernel<T, kGreedy><<<sgrid, kSThreads, smem_main, s>>>(a0);
+    else if (stream && mode == kTopK) stream_rows_kernel<T, kTopK><<<sgrid, kSThreads, smem_main, s>>>(a0);
+    else if (stream) stream_rows_kernel<T, kFullList><<<sgrid, kSThreads, smem_main, s>>>(a0);
+    else if (block_kernel) sample_rows_block_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
     else if (mode == kGreedy) sample_rows_kernel<T, kGreedy, 1><<<grid, kRowThreads, smem_main, s>>>(a0);
     else if (mode == kTopK && wide) sample_rows_kernel<T, kTopK, 4><<<grid, kRowThreads, smem_main, s>>>(a0);
     else if (mode == kTopK) sample_rows_kernel<T, kTopK, 1><<<grid, kRowThreads, smem_main, s>>>(a0);
@@ -335,9 +360,38 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         hist_bytes = W * 4 + (G + 1) * 4 + (size_t)(H - a.hist_start > 1 ? H - a.hist_start : 1) * 4;
         hist_bytes = (hist_bytes + 15) & ~size_t(15);
     }
-    size_t smem_main;
+    size_t smem_main = 0;
     bool wide = false;
-    if (block_kernel) {
+    /* the persistent streaming kernel wherever its ring fits next to the two
+     * row sets (greedy, top-k with K' <= 128, full lists); the ring needs more
+     * stages than there are consumer warps, since each warp's first stage of
+     * a row must be in the ring while the others wait for it */
+    bool stream = !block_kernel && ((kStreamModes >> mode) & 1u);
+    if (stream) {
+        if (a.penalty) {
+            const int win = H - a.hist_start > 1 ? H - a.hist_start : 1;
+            a.hcap = pow2_at_least(2 * win > 64 ? 2 * win : 64);
+        }
+        const StreamLayout l0 = stream_layout(mode, V, a.penalty, a.hcap, a.kprime, 0);
+        const size_t avail = c->smem_optin - kStreamStaticReserve;
+        const long long ns = l0.total < avail ? (long long)((avail - l0.total) / kStageBytes) : 0;
+        /* a multiple of the consumer pairs (each pair owns fixed stages), and
+         * more than one lap of them (a pair's first stage of a row must fit
+         * while the others wait for theirs) */
+        const long long ns4 = ((ns < kMaxStages ? ns : kMaxStages) / kGroups) * kGroups;
+        if (ns4 >= 2 * kGroups) {
+            a.nstages = (int)ns4;
+            a.wait_ns = t_wait_ns;
+            a.test_stall = t_stall_next;
+            t_stall_next = 0;
+            smem_main = stream_layout(mode, V, a.penalty, a.hcap, a.kprime, a.nstages).total;
+        } else {
+            stream = false;
+            a.hcap = 0;
+        }
+    }
+    if (stream) {
+    } else if (block_kernel) {
         /* the block kernel's history also holds the id of each rank while
          * it computes the penalised values */
         const size_t idr = a.penalty ? (size_t)(H - a.hist_start > 1 ? H - a.hist_start : 1) * 4 : 0;
@@ -386,8 +440,8 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         a.slots = w->slots;
         a.nslots = w->nslots;
     }
-    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, block_kernel, wide, smem_main, smem_exact, c, s)
-                                : launch_t<uint16_t>(a, mode, block_kernel, wide, smem_main, smem_exact, c, s);
+    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, block_kernel, wide, stream, smem_main, smem_exact, c, s)
+                                : launch_t<uint16_t>(a, mode, block_kernel, wide, stream, smem_main, smem_exact, c, s);
     if (r) return r;
     return ok();
 }
@@ -677,6 +731,25 @@ struct HostBatchStage {
     size_t ids_cap = 0;
     void *d_probs = nullptr;
     size_t probs_cap = 0;
+    /* the buffers and stream of the device they were made on, freed with
+     * that device current (a thread that moves to another device frees them
+     * first) */
+    void release() {
+        if (dev < 0) return;
+        int cur = -1;
+        cudaGetDevice(&cur);
+        cudaSetDevice(dev);
+        if (stream) cudaStreamSynchronize(stream);
+        cudaFree(d_logits);
+        cudaFree(d_hist);
+        cudaFree(d_rng);
+        cudaFree(d_ids);
+        cudaFree(d_probs);
+        if (stream) cudaStreamDestroy(stream);
+        if (cur >= 0) cudaSetDevice(cur);
+        *this = HostBatchStage{};
+    }
+    ~HostBatchStage() { release(); }
 };
 thread_local HostBatchStage t_hb;
 }  // namespace
@@ -748,12 +821,14 @@ extern "C" int noel_sampler_sample_batch_host(const noel_sampler_config_t *cfg, 
     if (!cfg || !h_logits || !h_rng || !h_ids || batch < 0 || vocab <= 0 || ld < (size_t)vocab)
         return fail(NOEL_ERR_INVALID_ARG, "invalid arguments");
     if (dtype != NOEL_DTYPE_F32 && dtype != NOEL_DTYPE_BF16) return fail(NOEL_ERR_INVALID_ARG, "dtype %d", dtype);
+    if (h_history && history_len > 0 && hld < (size_t)history_len)
+        return fail(NOEL_ERR_INVALID_ARG, "hld %zu < history_len %d", hld, history_len);
     if (batch == 0) return ok();
     HostBatchStage &st = t_hb;
     int dev = 0;
     CUDA_TRY(cudaGetDevice(&dev));
     if (st.dev != dev) {
-        st = HostBatchStage{};
+        st.release();
         st.dev = dev;
         CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
     }
@@ -810,6 +885,13 @@ extern "C" int noel_sampler_cuda_sync_check(void *stream) {
         CUDA_TRY(cudaMemset(flag, 0, sizeof(v)));
         return fail(NOEL_ERR_DEVICE_WAIT, "a device-side wait ran out of its limit");
     }
+    return ok();
+}
+
+extern "C" int noel_sampler_cuda_set_wait_limit(long long wait_ns, int stall_next_call) {
+    if (wait_ns < 0) return fail(NOEL_ERR_INVALID_ARG, "wait_ns %lld", wait_ns);
+    t_wait_ns = wait_ns == 0 ? kDefaultWaitNs : (unsigned long long)wait_ns;
+    t_stall_next = stall_next_call ? 1 : 0;
     return ok();
 }
 
@@ -884,7 +966,8 @@ int preset_attrs(DeviceCtx *c) {
     const void *ks[] = {(const void *)sample_rows_kernel<T, kGreedy, 1>, (const void *)sample_rows_kernel<T, kTopK, 1>,
                         (const void *)sample_rows_kernel<T, kTopK, 4>, (const void *)sample_rows_kernel<T, kFullList, 1>,
                         (const void *)sample_rows_kernel<T, kFullList, 4>, (const void *)sample_rows_block_kernel<T, kTopK>,
-                        (const void *)exact_rows_kernel<T>};
+                        (const void *)exact_rows_kernel<T>, (const void *)stream_rows_kernel<T, kGreedy>,
+                        (const void *)stream_rows_kernel<T, kTopK>, (const void *)stream_rows_kernel<T, kFullList>};
     for (const void *k : ks) {
         cudaFuncAttributes fa;
         CUDA_TRY(cudaFuncGetAttributes(&fa, k));

@@ -90,6 +90,10 @@ struct SampleArgs {
      * of a row of split_vocab columns; 0 or 1: rows are the caller's rows */
     int split, split_vocab;
     int qcap;                   // queued vectors per warp (single-pass kernel, queued modes)
+    /* persistent streaming kernel */
+    int nstages;                // shared-memory ring stages of 16 KB
+    int test_stall;             // 1: issue no row loads, so every wait runs out (failure-detection test)
+    unsigned long long wait_ns; // limit of every device-side wait (%globaltimer ns)
 };
 
 /* where kernel row r lives: element offset, columns, global id of its first

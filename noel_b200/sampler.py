@@ -124,6 +124,10 @@ def lib() -> C.CDLL:
     L.noel_sampler_cuda_profile_events.argtypes = [C.c_void_p, C.c_void_p]
     L.noel_sampler_cuda_expf_checksums.restype = C.c_int
     L.noel_sampler_cuda_expf_checksums.argtypes = [C.c_int, C.c_void_p, C.c_void_p]
+    L.noel_sampler_cuda_sync_check.restype = C.c_int
+    L.noel_sampler_cuda_sync_check.argtypes = [C.c_void_p]
+    L.noel_sampler_cuda_set_wait_limit.restype = C.c_int
+    L.noel_sampler_cuda_set_wait_limit.argtypes = [C.c_longlong, C.c_int]
     _lib = L
     return L
 
@@ -283,6 +287,22 @@ def profile_events(before=None, after=None) -> None:
             ev.record()  # torch creates the CUDA event on its first record
     lib().noel_sampler_cuda_profile_events(before.cuda_event if before is not None else None,
                                            after.cuda_event if after is not None else None)
+
+
+def sync_check(stream=None) -> int:
+    """Wait for ``stream`` (default: the current one) and return the status of
+    the device-side waits of the calls made on it (0, or NOEL_ERR_DEVICE_WAIT)."""
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(lib().noel_sampler_cuda_sync_check(C.c_void_p(s.cuda_stream)))
+
+
+def set_wait_limit(wait_ns: int = 0, stall_next_call: bool = False) -> None:
+    """Limit of the device-side waits of this thread's later batched calls
+    (0: the default, 2 s); ``stall_next_call`` makes the next call's kernel
+    issue no row loads so that its waits run out (failure-detection tests)."""
+    _check(lib().noel_sampler_cuda_set_wait_limit(int(wait_ns), 1 if stall_next_call else 0))
 
 
 def expf_table_size() -> int:

@@ -57,9 +57,19 @@ def make_config(temperature=0.7, top_p=0.9, top_k=40, repetition_penalty=1.1,
                          float(repetition_penalty), int(repetition_window), int(seed))
 
 
+def reference_root() -> str:
+    """The reference tree whose src/sampler.c oracle/_ref is built from:
+    $NOEL_REFERENCE_ROOT, else a directory named ``reference`` beside the
+    repository (absent on hosts that only run the prebuilt _ref/)."""
+    env = os.environ.get("NOEL_REFERENCE_ROOT")
+    if env:
+        return env
+    return os.path.abspath(os.path.join(HERE, "..", "..", "reference"))
+
+
 def build(quiet: bool = True) -> None:
     """Compile the checkers (``make -C oracle``)."""
-    out = subprocess.run(["make", "-C", HERE], capture_output=True, text=True)
+    out = subprocess.run(["make", "-C", HERE, f"REF_ROOT={reference_root()}"], capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
     if not quiet:

@@ -101,19 +101,20 @@ def test_workloads_full_vocab_gpu(cuda, oracle, case):
     assert_parity(name, g, o)
 
 
-@pytest.mark.parametrize("name", ["batch1024", "greedy_penalty", "nucleus_bf16"])
-def test_workloads_full_occupancy_gpu(cuda, oracle, name):
-    """Batches of up to two rows per SM (48 above) run the single-pass kernel
-    with wide batches at 2 CTAs per SM; 560 rows run it at 7-8 CTAs per SM,
-    the path of the full-size workloads."""
+@pytest.mark.parametrize("name,batch", [("batch1024", 1024), ("batch1024", 560), ("greedy_penalty", 560),
+                                        ("nucleus_bf16", 560)])
+def test_workloads_full_occupancy_gpu(cuda, oracle, name, batch):
+    """Batches that give every CTA of the streaming kernel several rows, so
+    both row sets of each CTA are reused; 1024 rows is the throughput
+    workload itself."""
     from noel_b200.workloads import WORKLOADS, generate_numpy
 
-    w = WORKLOADS[name].resized(batch=560)
+    w = WORKLOADS[name].resized(batch=batch)
     d = generate_numpy(w, seed=13)
     cfgkw = w.config_kwargs()
     o = oracle.sample_batch(orc_config(**cfgkw), d["logits"], history=d["history"], rng=d["rng"], n_list=64)
     g = run_gpu(cuda, cfgkw, d["logits"], d["history"], d["rng"])
-    assert_parity(f"{name}/560", g, o)
+    assert_parity(f"{name}/{batch}", g, o)
 
 
 @pytest.mark.parametrize("top_k,T", [(500, 0.9), (40, 0.8), (1, 0.0), (0, 1.0)])

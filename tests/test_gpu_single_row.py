@@ -76,3 +76,31 @@ def test_single_row_matches_oracle_gpu(cuda, oracle, case):
             cands = sm.candidates(min(n, 64))
             assert [c[0] for c in cands] == list(o.topn_ids[0, : len(cands)])
     sm.free()
+
+
+def test_single_row_host_logits_device_history_gpu(cuda, oracle):
+    """Host logits with a device history: the kernel penalises the staged row
+    and the whole penalised row comes back into the caller's host buffer
+    (sampler.c:87-103 mutates the caller's logits)."""
+    import torch
+
+    from noel_b200 import sampler as S
+
+    name, cfgkw, x0, hist = rows()[0]
+    cfgkw = dict(cfgkw, seed=77)
+    sm = S.Sampler(S.make_config(**cfgkw), len(x0))
+    st = np.array([list(sm.rng_state)], np.uint64)
+    x = x0.copy()
+    hd = torch.from_numpy(hist.copy()).to(cuda)
+    for step in range(2):
+        o = oracle.sample_batch(orc_config(**cfgkw), x[None].copy(), history=hist[None], rng=st, n_list=64)
+        want_after = penalised(x, hist, cfgkw["repetition_penalty"], cfgkw["repetition_window"])
+        got = sm.sample(x, hd)
+        assert got == o.ids[0], f"step {step}"
+        st = o.rng
+        assert sm.rng_state == (int(st[0, 0]), int(st[0, 1]))
+        np.testing.assert_array_equal(x.view(np.uint32), want_after.view(np.uint32), err_msg="write-back")
+        n = int(o.diag["n_final"][0])
+        cands = sm.candidates(min(n, 64))
+        assert [c[0] for c in cands] == list(o.topn_ids[0, : len(cands)])
+    sm.free()
