@@ -3,19 +3,20 @@
  * another (rows b, b + G, b + 2G, ... for CTA b of G), so that every phase of
  * a row other than reading it overlaps the reading of the next one.
  *
- * Warp roles (one CTA of 11 warps):
+ * Warp roles (one CTA of 19 warps):
  *   producer   (warp 0)    one lane issues cp.async.bulk copies of the rows'
  *                          16-byte-aligned bodies, 16 KB at a time, into a
  *                          ring of shared-memory stages; each stage has a
  *                          "full" mbarrier (transaction bytes) and an "empty"
  *                          one (released by the consumers).  The stream never
  *                          stops at a row boundary.
- *   consumers  (warps 1-8) stages go to four pairs of consumer warps in turn
- *                          (stage k of the stream to pair k mod 4, one 8 KB
- *                          half per warp), so four stages are read at once; a
- *                          lane reads sixteen 16-byte pieces of its half (64
- *                          fp32 or 128 bf16 elements) and compares their raw
- *                          maxima with the row's current filter.  Only a
+ *   consumers  (warps 1-16) stages go to four groups of four consumer warps
+ *                          in turn (stage k of the stream to group k mod 4,
+ *                          one 4 KB quarter per warp), so four stages are read
+ *                          at once; a lane reads eight 16-byte pieces of its
+ *                          quarter (32 fp32 or 64 bf16 elements) and compares
+ *                          their raw maxima with the row's current filter.
+ *                          Only a
  *                          piece that can pass is penalised (the penalty only
  *                          lowers values, sampler.c:96-100) and tested
  *                          element by element, by its own lane, one such
@@ -28,7 +29,7 @@
  *                            full    elements within the -15 cut under the
  *                                    running maximum (sampler.c:119-143) are
  *                                    appended.
- *   finishers  (warps 9-10) finisher f owns row set f (every other row of the
+ *   finishers  (warps 17-18) finisher f owns row set f (every other row of the
  *                          CTA): the row state, the history table and the
  *                          candidate buffer.  It prepares a row (history
  *                          bitmap and penalised values, the unaligned head and
@@ -64,16 +65,16 @@
 
 namespace noel {
 
-constexpr int kSCons = 8;                        // consumer warps
+constexpr int kSCons = 16;                       // consumer warps
 constexpr int kSFin = 2;                         // finisher warps = row sets
 constexpr int kSWarps = 1 + kSCons + kSFin;
 constexpr int kSThreads = 32 * kSWarps;
 constexpr int kStageBytes = 16384;               // one stage: one bulk copy
-constexpr int kParts = 2;                        // consumer warps sharing a stage
-/* Stages read at once: stage s belongs to pair s mod kGroups, and the ring's
- * stage count is a multiple of kGroups, so a pair sees every fill of its own
- * stages in order.  (A pair waiting on a stage whose previous fill belonged to
- * another pair could find that fill still pending, and the parity of the fill
+constexpr int kParts = 4;                        // consumer warps sharing a stage
+/* Stages read at once: stage s belongs to group s mod kGroups, and the ring's
+ * stage count is a multiple of kGroups, so a group sees every fill of its own
+ * stages in order.  (A group waiting on a stage whose previous fill belonged to
+ * another group could find that fill still pending, and the parity of the fill
  * it wants equals the parity of the one before: try_wait would pass a phase
  * early.) */
 constexpr int kGroups = kSCons / kParts;
@@ -83,7 +84,7 @@ constexpr int kMaxStages = 16;
 constexpr int kRowBuf = 1024;                    // candidate entries per row set
 constexpr int kFullSortMax = 512;                // full-list candidates a finisher sorts itself
 constexpr int kLadders = 4;                      // warm-up ladder slots per consumer warp
-static_assert(kPieces == 16, "sixteen 16-byte pieces per lane");
+static_assert(kPieces == 8, "eight 16-byte pieces per lane");
 
 /* state of one row set, shared by the consumers and the set's finisher */
 struct StreamRow {
@@ -286,10 +287,10 @@ __device__ __forceinline__ SetView set_view(unsigned char *smem, const StreamLay
  * slots whose filter is >= f) */
 __device__ __forceinline__ unsigned long long ladder_combine(const StreamRow &st, int kprime) {
     const int lane = threadIdx.x & 31;
-    unsigned long long cand = 0ull;
-    if (lane < kLadders * kSCons) cand = *(volatile const unsigned long long *)&st.lf[lane / kSCons][lane % kSCons];
     unsigned long long r = 0ull;
-    if (cand) {
+    for (int c = lane; c < kLadders * kSCons; c += 32) {  // every published filter is a candidate
+        const unsigned long long cand = *(volatile const unsigned long long *)&st.lf[c / kSCons][c % kSCons];
+        if (!cand || cand <= r) continue;
         int tot = 0;
         for (int w = 0; w < kSCons; ++w) {
             int best = 0;
@@ -868,7 +869,7 @@ __device__ void stream_consume(const SampleArgs &a, StreamShared &sh, unsigned c
     unsigned char *ring = smem;
     int s = 0;          // ring stage of the next chunk, as the producer counts it
     uint32_t ph = 0u;   // its fill's phase parity
-    int og = 0;         // consumer pair owning the next chunk
+    int og = 0;         // consumer group owning the next chunk
     int j = 0;
     for (int row = blockIdx.x; row < a.batch; row += G, ++j) {
         const int f = j & 1;
@@ -893,7 +894,7 @@ __device__ void stream_consume(const SampleArgs &a, StreamShared &sh, unsigned c
         };
 
         if (MODE != kGreedy) {
-            /* warm-up: this warp's part of its pair's first chunk of the row
+            /* warm-up: this warp's part of its group's first chunk of the row
              * (c0 < 4 < S, so it is at most one lap ahead in the ring) */
             const int c0 = grp >= og ? grp - og : grp + kGroups - og;
             float lm = -INFINITY;
@@ -1036,7 +1037,7 @@ __global__ void __launch_bounds__(kSThreads, 1) stream_rows_kernel(const __grid_
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mb_init(&sh.full[s], 1);
-            mb_init(&sh.empty[s], kParts);  // released by the stage's pair of consumer warps
+            mb_init(&sh.empty[s], kParts);  // released by the stage's group of consumer warps
         }
         for (int f = 0; f < kSFin; ++f) {
             mb_init(&sh.ready[f], 1);
