@@ -172,10 +172,16 @@ int pow2_at_least(int x) {
 }
 
 constexpr int kMaxKprime = 1024;     // top-k mode up to k = 1016
-constexpr size_t kStreamStaticReserve = 4096;  // static shared memory of the streaming kernel, rounded up
-/* modes the persistent streaming kernel serves (the others use the one-CTA-
- * per-row kernels, measured faster for them so far) */
-constexpr unsigned kStreamModes = 1u << kFullList;
+constexpr size_t kStreamStaticReserve = 10240;  // static shared memory of the streaming kernel, rounded up
+static_assert(sizeof(StreamShared) <= kStreamStaticReserve, "streaming kernel's static shared memory");
+/* modes the persistent streaming kernel serves; the others use the one-CTA-
+ * per-row kernels, measured faster for them on B200 (1024 x 152,064 fp32:
+ * top-k 40 with a penalty 166 vs 281 us, greedy 113 vs 174 us).  A build
+ * with -DNOEL_STREAM_MODES=7 streams every mode (all parity tests pass). */
+#ifndef NOEL_STREAM_MODES
+#define NOEL_STREAM_MODES (1u << kFullList)
+#endif
+constexpr unsigned kStreamModes = NOEL_STREAM_MODES;
 constexpr int kWarpKprimeMax = 128;  // warp-streaming kernel up to k = 120
 constexpr int kCapMax = 4096;
 
@@ -362,10 +368,8 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     }
     size_t smem_main = 0;
     bool wide = false;
-    /* the persistent streaming kernel wherever its ring fits next to the two
-     * row sets (greedy, top-k with K' <= 128, full lists); the ring needs more
-     * stages than there are consumer warps, since each warp's first stage of
-     * a row must be in the ring while the others wait for it */
+    /* the persistent streaming kernel wherever its ring fits next to the
+     * four row sets (greedy, top-k with K' <= 128, full lists) */
     bool stream = !block_kernel && ((kStreamModes >> mode) & 1u);
     if (stream) {
         if (a.penalty) {
@@ -375,12 +379,11 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         const StreamLayout l0 = stream_layout(mode, V, a.penalty, a.hcap, a.kprime, 0);
         const size_t avail = c->smem_optin - kStreamStaticReserve;
         const long long ns = l0.total < avail ? (long long)((avail - l0.total) / kStageBytes) : 0;
-        /* a multiple of the consumer pairs (each pair owns fixed stages), and
-         * more than one lap of them (a pair's first stage of a row must fit
-         * while the others wait for theirs) */
-        const long long ns4 = ((ns < kMaxStages ? ns : kMaxStages) / kGroups) * kGroups;
-        if (ns4 >= 2 * kGroups) {
-            a.nstages = (int)ns4;
+        /* at least the chunks a finisher reads for a row's starting filter
+         * plus one chunk per consumer group */
+        const long long nsc = ns < kMaxStages ? ns : kMaxStages;
+        if (nsc >= kMinStages) {
+            a.nstages = (int)nsc;
             a.wait_ns = t_wait_ns;
             a.test_stall = t_stall_next;
             t_stall_next = 0;

@@ -1,26 +1,27 @@
 /*
  * The persistent streaming kernel: one CTA per SM walks its rows one after
  * another (rows b, b + G, b + 2G, ... for CTA b of G), so that every phase of
- * a row other than reading it overlaps the reading of the next one.
+ * a row other than reading it overlaps the reading of other rows.
  *
- * Warp roles (one CTA of 19 warps):
+ * Warp roles (one CTA of 21 warps):
  *   producer   (warp 0)    one lane issues cp.async.bulk copies of the rows'
  *                          16-byte-aligned bodies, 16 KB at a time, into a
  *                          ring of shared-memory stages; each stage has a
  *                          "full" mbarrier (transaction bytes) and an "empty"
  *                          one (released by the consumers).  The stream never
- *                          stops at a row boundary.
- *   consumers  (warps 1-16) stages go to four groups of four consumer warps
- *                          in turn (stage k of the stream to group k mod 4,
+ *                          stops at a row boundary.  A shared counter of the
+ *                          copies issued so far tells a waiter which fill of a
+ *                          stage its parity refers to.
+ *   consumers  (warps 1-16) chunks of the stream go to four groups of four
+ *                          consumer warps in turn (chunk q to group q mod 4,
  *                          one 4 KB quarter per warp), so four stages are read
  *                          at once; a lane reads eight 16-byte pieces of its
  *                          quarter (32 fp32 or 64 bf16 elements) and compares
  *                          their raw maxima with the row's current filter.
- *                          Only a
- *                          piece that can pass is penalised (the penalty only
- *                          lowers values, sampler.c:96-100) and tested
- *                          element by element, by its own lane, one such
- *                          piece per lane per round:
+ *                          Only a piece that can pass is penalised (the
+ *                          penalty only lowers values, sampler.c:96-100) and
+ *                          tested element by element, by its own lane, one
+ *                          such piece per lane per round:
  *                            greedy  per-lane (value desc, id asc) best
  *                                    (sampler.c:105-116);
  *                            top-k   elements above the row's shared filter
@@ -29,30 +30,42 @@
  *                            full    elements within the -15 cut under the
  *                                    running maximum (sampler.c:119-143) are
  *                                    appended.
- *   finishers  (warps 17-18) finisher f owns row set f (every other row of the
- *                          CTA): the row state, the history table and the
- *                          candidate buffer.  It prepares a row (history
+ *                          Apart from its group's warm-up meeting, a consumer
+ *                          warp never waits for the others: it goes from one
+ *                          row to the next as soon as the next row's set is
+ *                          ready.
+ *   finishers  (warps 17-20) finisher f owns row set f (rows j = f, f + 4, ...
+ *                          of the CTA): the row state, the history table and
+ *                          the candidate buffer.  It prepares a row (history
  *                          bitmap and penalised values, the unaligned head and
- *                          tail elements, NaN at id 0) before the consumers
- *                          reach it.  While its row streams it keeps the
- *                          top-k filter tight: a two-pass radix count over the
- *                          keys appended so far gives a 16-bit key prefix with
- *                          at least K' of them at or above it.  When the row
- *                          has streamed it runs the row end: selection of the
- *                          K' best, weights and the sequential mass / nucleus
- *                          / draw of sampler.c:155-191, or the K' best of a
- *                          vocab shard.
+ *                          tail elements, NaN at id 0) while the consumers
+ *                          still read the rows before it.  While its row
+ *                          streams it keeps the top-k filter tight: a two-pass
+ *                          radix count over the keys appended so far gives a
+ *                          16-bit key prefix with at least K' of them at or
+ *                          above it.  When the row has streamed it runs the
+ *                          row end: selection of the K' best, weights and the
+ *                          sequential mass / nucleus / draw of
+ *                          sampler.c:155-191, or the K' best of a vocab shard.
+ *                          With four sets, a row end and the next preparation
+ *                          of its set overlap the streaming of three rows.
  *
- * Start of a row (top-k and full): the consumers take the maxima of their
- * lanes over the row's first stage, publish ladders of them (top-k) or their
- * maximum (full) and meet once on an mbarrier; the combined ladders give the
- * starting filter.
+ * Starting filter: each consumer warp first takes its lanes' maxima over
+ * pieces of its group's first chunk of the row that hold no history id (their
+ * values are final).  Full list: the largest starts the running maximum.
+ * Top-k: the group's four warps meet (one mbarrier per group, no wait for the
+ * other groups), each raises the filter to the K'-th largest of their 128
+ * lane maxima, and the group publishes a ladder of them to the row set; every
+ * group then combines all ladders published so far (K' lane maxima across
+ * groups above a value), so the last group to arrive sets a filter from all
+ * four chunks.  Every lane maximum is an element that passes the filter when
+ * its group reads the chunk.
  *
  * Exactness: every element that reaches the buffer stays there, and every
- * filter value f has at least K' buffered elements with composite key >= f,
- * so an element left out ranks below K' others.  A buffer that overflows, or
- * a tie of weights at the top-k boundary, sends the row to the two-pass
- * kernel.
+ * filter value f has at least K' elements with composite key >= f that reach
+ * the buffer (or, for a raised filter, are in it), so an element left out
+ * ranks below K' others.  A buffer that overflows, or a tie of weights at the
+ * top-k boundary, sends the row to the two-pass kernel.
  *
  * Every wait is bounded (SampleArgs::wait_ns of %globaltimer): a wait that
  * runs out sets counters[3] and the CTA's error flag, every role leaves its
@@ -66,30 +79,27 @@
 namespace noel {
 
 constexpr int kSCons = 16;                       // consumer warps
-constexpr int kSFin = 2;                         // finisher warps = row sets
+constexpr int kSFin = 4;                         // finisher warps = row sets
 constexpr int kSWarps = 1 + kSCons + kSFin;
 constexpr int kSThreads = 32 * kSWarps;
 constexpr int kStageBytes = 16384;               // one stage: one bulk copy
-constexpr int kParts = 4;                        // consumer warps sharing a stage
-/* Stages read at once: stage s belongs to group s mod kGroups, and the ring's
- * stage count is a multiple of kGroups, so a group sees every fill of its own
- * stages in order.  (A group waiting on a stage whose previous fill belonged to
- * another group could find that fill still pending, and the parity of the fill
- * it wants equals the parity of the one before: try_wait would pass a phase
- * early.) */
-constexpr int kGroups = kSCons / kParts;
-constexpr int kPartBytes = kStageBytes / kParts; // one consumer warp's part of a stage
-constexpr int kPieces = kPartBytes / (16 * 32);  // 16-byte pieces per lane and stage
+constexpr int kParts = 4;                        // consumer warps sharing a chunk
+constexpr int kGroups = kSCons / kParts;         // chunks read at once
+constexpr int kPartBytes = kStageBytes / kParts; // one consumer warp's part of a chunk
+constexpr int kPieces = kPartBytes / (16 * 32);  // 16-byte pieces per lane and part
 constexpr int kMaxStages = 16;
+constexpr int kMinStages = 8;                    // two chunks per consumer group
 constexpr int kRowBuf = 1024;                    // candidate entries per row set
 constexpr int kFullSortMax = 512;                // full-list candidates a finisher sorts itself
-constexpr int kLadders = 4;                      // warm-up ladder slots per consumer warp
 static_assert(kPieces == 8, "eight 16-byte pieces per lane");
 
 /* state of one row set, shared by the consumers and the set's finisher */
+constexpr int kLadders = 4;                      // ladder slots a group publishes per row
+
 struct StreamRow {
     unsigned long long tsh;             // top-k filter: an element passes iff comp_key > tsh
-    unsigned long long lf[kLadders][kSCons];  // warm-up ladders; slot j counts ladder_count(j) elements
+    unsigned long long lad[kGroups][kLadders];  // group g's ladder: slot i has ladder_count(i) lane maxima above it
+    uint32_t pub;                       // groups whose ladder is published
     float gx[kSCons];                   // greedy: each warp's best
     uint32_t gid[kSCons];
     float sgx;                          // greedy: best head / tail element
@@ -103,8 +113,10 @@ struct StreamShared {
     unsigned long long full[kMaxStages], empty[kMaxStages];
     unsigned long long ready[kSFin];    // finisher -> consumers: set prepared for its next row
     unsigned long long done[kSFin];     // consumers -> finisher: row streamed
-    unsigned long long warm[kSFin];     // consumers meet after publishing the first stage's ladders
+    unsigned long long gmeet[kGroups];  // a group's four warps meet once per row (top-k warm-up)
+    unsigned long long glad[2][kGroups][kParts][32];  // their sorted lane maxima, by row parity
     StreamRow st[kSFin];
+    uint32_t issued;                    // chunks the producer has issued (release / acquire)
     int err;
 };
 
@@ -166,6 +178,15 @@ __device__ __forceinline__ uint64_t gtimer() {
     return t;
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_shared(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(sm_addr(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_shared(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(sm_addr(p)), "r"(v) : "memory");
+}
+
 /* One thread's bounded wait for the phase of the given parity.  False when
  * the limit ran out (flags set) or another role gave up. */
 __device__ __noinline__ bool mb_wait_thread(unsigned long long *b, uint32_t parity, const SampleArgs &a,
@@ -196,6 +217,32 @@ __device__ __forceinline__ bool mb_wait_warp(unsigned long long *b, uint32_t par
     for (int i = 0; i < (1 << 20) && !mb_try(b, parity); ++i) {
     }
     return true;
+}
+
+/* A warp's bounded wait for chunk q of the CTA's stream (stage q mod S, fill
+ * q / S).  The producer issues chunk q only after the stage's previous fill
+ * was released, so once the issue counter has passed q the stage's barrier
+ * is in the phase of fill q / S or past it, and the parity names that fill. */
+__device__ __forceinline__ bool chunk_wait(uint32_t q, int S, const SampleArgs &a, StreamShared &sh) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0 && ld_acquire_shared(&sh.issued) <= q) {
+        const uint64_t t0 = gtimer();
+        while (ld_acquire_shared(&sh.issued) <= q) {
+            if (*(volatile int *)&sh.err) {
+                ok = 0;
+                break;
+            }
+            if (gtimer() - t0 > a.wait_ns) {
+                sh.err = 1;
+                atomicExch(&a.counters[3], 1);
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!__shfl_sync(kFull, ok, 0)) return false;
+    return mb_wait_warp(&sh.full[q % (uint32_t)S], (q / (uint32_t)S) & 1u, a, sh);
 }
 
 /* ---------------------------------------------------------------------- */
@@ -258,9 +305,39 @@ __host__ __device__ inline StreamLayout stream_layout(int mode, int vocab, int p
     return L;
 }
 
-/* warm-up ladder slot j counts (j + 1) K'/16 lane maxima (at most 32, so the
- * first stage's 32 lane maxima of a warp can fill every slot) */
-__device__ __forceinline__ int ladder_count(int j, int kprime) { return max(1, kprime / 16) * (j + 1); }
+/* warm-up ladder slot i counts (i + 1) K' / 4 lane maxima of a group (at
+ * most its 128) */
+__device__ __forceinline__ int ladder_count(int i, int kprime) { return max(1, kprime / kLadders) * (i + 1); }
+
+/* The largest published ladder value f such that the published groups hold
+ * at least K' lane maxima above it (summing, over groups, the largest count
+ * among that group's slots whose value is >= f); 0 if none. */
+__device__ __forceinline__ unsigned long long ladder_pool(const StreamRow &st, uint32_t pub, int kprime) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long r = 0ull;
+    if (lane < kGroups * kLadders && ((pub >> (lane / kLadders)) & 1u)) {
+        const unsigned long long cand = *(volatile const unsigned long long *)&st.lad[lane / kLadders][lane % kLadders];
+        int tot = 0;
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g) {
+            if (!((pub >> g) & 1u)) continue;
+            int best = 0;
+#pragma unroll
+            for (int i = 0; i < kLadders; ++i) {
+                const unsigned long long f = *(volatile const unsigned long long *)&st.lad[g][i];
+                if (f && f >= cand) best = ladder_count(i, kprime);
+            }
+            tot += best;
+        }
+        if (cand && tot >= kprime) r = cand;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(kFull, r, o);
+        r = t > r ? t : r;
+    }
+    return r;
+}
 
 /* views of a set */
 struct SetView {
@@ -280,35 +357,6 @@ __device__ __forceinline__ SetView set_view(unsigned char *smem, const StreamLay
     v.bkey = reinterpret_cast<uint32_t *>(base + L.bkey);
     v.bid = reinterpret_cast<uint32_t *>(base + L.bid);
     return v;
-}
-
-/* the largest published ladder filter f with at least K' lane maxima at or
- * above it in all (sum over warps of the largest count among that warp's
- * slots whose filter is >= f) */
-__device__ __forceinline__ unsigned long long ladder_combine(const StreamRow &st, int kprime) {
-    const int lane = threadIdx.x & 31;
-    unsigned long long r = 0ull;
-    for (int c = lane; c < kLadders * kSCons; c += 32) {  // every published filter is a candidate
-        const unsigned long long cand = *(volatile const unsigned long long *)&st.lf[c / kSCons][c % kSCons];
-        if (!cand || cand <= r) continue;
-        int tot = 0;
-        for (int w = 0; w < kSCons; ++w) {
-            int best = 0;
-#pragma unroll
-            for (int j = 0; j < kLadders; ++j) {
-                const unsigned long long f = *(volatile const unsigned long long *)&st.lf[j][w];
-                if (f && f >= cand) best = max(best, ladder_count(j, kprime));
-            }
-            tot += best;
-        }
-        if (tot >= kprime) r = cand;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long t = __shfl_xor_sync(kFull, r, o);
-        r = t > r ? t : r;
-    }
-    return r;
 }
 
 /* one 16-byte piece as PE floats (fp32, or bf16 widened exactly) */
@@ -412,6 +460,15 @@ __device__ void hs_build_warp(const HistSet &h, const int32_t *hrow, int first, 
     __syncwarp();
 }
 
+/* the consumers' float bound of a top-k filter: a piece can pass only if its
+ * raw maximum reaches it (a prefix at or below -inf's key bounds nothing) */
+__device__ __forceinline__ float filter_bound(unsigned long long te) {
+    const uint32_t hi = (uint32_t)(te >> 32);
+    return hi <= kKeyNegInf ? -INFINITY : key_float(hi);
+}
+
+/* Prepare a row of the set: its state, the history table, the unaligned head
+ * and tail elements and NaN at id 0. */
 template <typename T, int MODE>
 __device__ __noinline__ void stream_prepare(const SampleArgs &a, StreamRow &st, const SetView &v, int row) {
     using F = Fmt<T>;
@@ -419,8 +476,6 @@ __device__ __noinline__ void stream_prepare(const SampleArgs &a, StreamRow &st, 
     const RowSpan span = row_span(a, row);
     const void *rowp = static_cast<const char *>(a.logits) + (size_t)span.off * F::ES;
     if (lane < kSCons) {
-#pragma unroll
-        for (int jj = 0; jj < kLadders; ++jj) st.lf[jj][lane] = 0ull;
         st.gx[lane] = -INFINITY;
         st.gid[lane] = 0xFFFFFFFFu;
     }
@@ -431,14 +486,14 @@ __device__ __noinline__ void stream_prepare(const SampleArgs &a, StreamRow &st, 
     uint32_t ids = have ? (uint32_t)bulk_scalar_id(g, lane) : 0u;
     float xs = have ? F::scalar(rowp, (int)ids) : 0.0f;
     const float x0 = lane == 0 ? F::scalar(rowp, 0) : 0.0f;
+    if (lane < kGroups * kLadders) st.lad[lane / kLadders][lane % kLadders] = 0ull;
     if (lane == 0) {
+        st.pub = 0u;
         st.tsh = 0ull;
         st.maxkey = kKeyNegInf;
         st.cnt = 0;
         st.l0nan = x0 != x0;  // the penalty keeps a NaN a NaN
     }
-    if (MODE == kTopK)  // unwritten entries read as key 0 while the filter is refreshed
-        for (int i = lane; i < kRowBuf / 4; i += 32) reinterpret_cast<uint4 *>(v.bkey)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (a.penalty)
         hs_build_warp<T>(v.hs, a.hist + (size_t)span.hrow * a.hld, a.hist_start, a.hist_len, span.V, span.id_off, rowp,
                          a.rep);
@@ -463,19 +518,24 @@ __device__ __noinline__ void stream_prepare(const SampleArgs &a, StreamRow &st, 
             st.sgx = bx;
             st.sgid = bid;
         }
-    } else {
-        const bool ins = have && xs == xs;
-        const uint32_t b = __ballot_sync(kFull, ins);
-        if (ins) {
-            const int pos = __popc(b & lanemask_lt());
-            v.bkey[pos] = ord_key(xs);
-            v.bid[pos] = ids;
-        }
-        if (lane == 0) st.cnt = __popc(b);
-        if (MODE == kFullList) {
-            const float m = warp_max_f(ins ? xs : -INFINITY);
-            if (lane == 0 && m > -INFINITY) st.maxkey = max(st.maxkey, ord_key(m));
-        }
+        __syncwarp();
+        return;
+    }
+
+    if (MODE == kTopK)  // unwritten entries read as key 0 while the filter is refreshed
+        for (int i = lane; i < kRowBuf / 4; i += 32) reinterpret_cast<uint4 *>(v.bkey)[i] = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
+    const bool ins = have && xs == xs;
+    const uint32_t b = __ballot_sync(kFull, ins);
+    if (ins) {
+        const int pos = __popc(b & lanemask_lt());
+        v.bkey[pos] = ord_key(xs);
+        v.bid[pos] = ids;
+    }
+    if (lane == 0) st.cnt = __popc(b);
+    if (MODE == kFullList) {
+        const float m = warp_max_f(ins ? xs : -INFINITY);
+        if (lane == 0 && m > -INFINITY) st.maxkey = max(st.maxkey, ord_key(m));
     }
     __syncwarp();
 }
@@ -867,140 +927,161 @@ __device__ void stream_consume(const SampleArgs &a, StreamShared &sh, unsigned c
     const int S = a.nstages;
     const int grp = cw / kParts, part = cw % kParts;
     unsigned char *ring = smem;
-    int s = 0;          // ring stage of the next chunk, as the producer counts it
-    uint32_t ph = 0u;   // its fill's phase parity
-    int og = 0;         // consumer group owning the next chunk
+    uint32_t q = 0u;  // the next chunk of the CTA's stream
     int j = 0;
     for (int row = blockIdx.x; row < a.batch; row += G, ++j) {
-        const int f = j & 1;
-        const uint32_t use = (uint32_t)(j >> 1) & 1u;
+        const int f = j % kSFin;
+        const uint32_t use = (uint32_t)(j / kSFin) & 1u;
         StreamRow &st = sh.st[f];
         if (!mb_wait_warp(&sh.ready[f], use, a, sh)) return;
         const SetView v = set_view(smem, L, a, f);
         const RowSpan span = row_span(a, row);
         const void *rowp = static_cast<const char *>(a.logits) + (size_t)span.off * F::ES;
         const BulkGeom g = bulk_geom<T>(rowp, span.V);
-        /* this warp's bytes of chunk c, and the id of its lane's first element */
-        auto part_bytes = [&](int c) -> int {
-            const long long rem = g.body - (long long)c * kStageBytes - (long long)part * kPartBytes;
-            return rem <= 0 ? 0 : (int)min((long long)kPartBytes, rem);
-        };
-        auto part_id = [&](int c) -> uint32_t {
-            return (uint32_t)(g.head + ((long long)c * kStageBytes + (long long)part * kPartBytes) / ES) +
-                   (uint32_t)(lane * PE);
-        };
-        auto pbase = [&](int st_) -> const unsigned char * {
-            return ring + (size_t)st_ * kStageBytes + (size_t)part * kPartBytes;
-        };
 
+        float gx = -INFINITY;
+        uint32_t gid = 0xFFFFFFFFu;
+        /* this group's chunks of the row: chunk c is stream chunk q + c */
+        const int c0 = (int)(((uint32_t)grp + kGroups - q % kGroups) % kGroups);
         if (MODE != kGreedy) {
-            /* warm-up: this warp's part of its group's first chunk of the row
-             * (c0 < 4 < S, so it is at most one lap ahead in the ring) */
-            const int c0 = grp >= og ? grp - og : grp + kGroups - og;
+            /* warm-up on the group's first chunk of the row: lane maxima over
+             * pieces holding no history id (final values).  Full list: their
+             * maximum starts the running maximum.  Top-k: the group's four
+             * warps meet and take the K'-th largest of their 128 lane maxima,
+             * less one, as a filter; those K' elements pass it when the group
+             * reads the chunk next. */
             float lm = -INFINITY;
             uint32_t lid = 0xFFFFFFFFu;
             if (c0 < g.nchunks) {
-                const int s0 = s + c0 >= S ? s + c0 - S : s + c0;
-                const uint32_t p0 = s + c0 >= S ? ph ^ 1u : ph;
-                if (!mb_wait_warp(&sh.full[s0], p0, a, sh)) return;
-                part_scan<T, true>(pbase(s0), part_bytes(c0), part_id(c0), v.hs, a.penalty != 0,
-                                   [](float) { return false; }, lm, lid);
+                const uint32_t qc = q + (uint32_t)c0;
+                if (!chunk_wait(qc, S, a, sh)) return;
+                const long long rem = g.body - (long long)c0 * kStageBytes - (long long)part * kPartBytes;
+                const int nbw = rem <= 0 ? 0 : (int)min((long long)kPartBytes, rem);
+                const uint32_t id_lane =
+                    (uint32_t)(g.head + ((long long)c0 * kStageBytes + (long long)part * kPartBytes) / ES) +
+                    (uint32_t)(lane * PE);
+                part_scan<T, true>(ring + (size_t)(qc % (uint32_t)S) * kStageBytes + (size_t)part * kPartBytes, nbw,
+                                   id_lane, v.hs, a.penalty != 0, [](float) { return false; }, lm, lid);
             }
             if (MODE == kTopK) {
                 uint64_t k1[1] = {lid != 0xFFFFFFFFu ? comp_key(ord_key(lm), lid) : 0ull};
                 warp_sort_desc<1>(k1);
-                /* sorted position i is lane i; slot jj holds the
-                 * ladder_count(jj)-th largest lane maximum, less one (those
-                 * lane maxima pass a filter below them) */
+                unsigned long long(*gl)[32] = sh.glad[j & 1][grp];
+                gl[part][lane] = k1[0];
+                __syncwarp();
+                if (lane == 0) mb_arrive(&sh.gmeet[grp]);
+                if (!mb_wait_warp(&sh.gmeet[grp], (uint32_t)j & 1u, a, sh)) return;
+                uint64_t k4[kParts];
 #pragma unroll
-                for (int jj = 0; jj < kLadders; ++jj) {
-                    const uint64_t kk = __shfl_sync(kFull, k1[0], ladder_count(jj, a.kprime) - 1);
-                    if (lane == 0) *(volatile unsigned long long *)&st.lf[jj][cw] = kk ? kk - 1ull : 0ull;
+                for (int w = 0; w < kParts; ++w) k4[w] = gl[w][lane];
+                warp_sort_desc<kParts>(k4);
+                /* sorted position p sits in lane p / kParts, slot p % kParts;
+                 * ladder slot i is the value at position ladder_count(i) - 1,
+                 * less one (those lane maxima pass a filter below them) */
+                {
+                    /* every warp of the group: the group's own filter (K'-th
+                     * of its 128 lane maxima) before it reads the chunk */
+                    const int pk = min(a.kprime, kParts * 32) - 1;
+                    uint64_t kk = 0ull;
+#pragma unroll
+                    for (int w = 0; w < kParts; ++w)
+                        if (w == pk % kParts) kk = k4[w];
+                    kk = __shfl_sync(kFull, kk, pk / kParts);
+                    if (lane == 0 && kk && a.kprime <= kParts * 32) atomicMax(&st.tsh, kk - 1ull);
+                }
+                if (part == 0) {
+#pragma unroll
+                    for (int i = 0; i < kLadders; ++i) {
+                        const int pk = min(ladder_count(i, a.kprime), kParts * 32) - 1;
+                        uint64_t kk = 0ull;
+#pragma unroll
+                        for (int w = 0; w < kParts; ++w)
+                            if (w == pk % kParts) kk = k4[w];
+                        kk = __shfl_sync(kFull, kk, pk / kParts);
+                        if (lane == 0)
+                            st.lad[grp][i] = (kk && ladder_count(i, a.kprime) <= kParts * 32) ? kk - 1ull : 0ull;
+                    }
+                    __syncwarp();
+                    __threadfence_block();
+                    uint32_t pub = 0u;
+                    if (lane == 0) pub = atomicOr(&st.pub, 1u << grp) | (1u << grp);
+                    pub = __shfl_sync(kFull, pub, 0);
+                    __threadfence_block();
+                    const unsigned long long pf = ladder_pool(st, pub, a.kprime);
+                    if (lane == 0 && pf) atomicMax(&st.tsh, pf);
                 }
             } else {
-                const float m = warp_max_f(lm);
+                const float m = warp_max_f(lid != 0xFFFFFFFFu ? lm : -INFINITY);
                 if (lane == 0 && m > -INFINITY) atomicMax(&st.maxkey, ord_key(m));
             }
-            __syncwarp();
-            if (lane == 0) mb_arrive(&sh.warm[f]);
-            if (!mb_wait_warp(&sh.warm[f], use, a, sh)) return;
-            if (MODE == kTopK) {
-                const unsigned long long cmb = ladder_combine(st, a.kprime);
-                if (lane == 0 && cmb) atomicMax(&st.tsh, cmb);
-            }
         }
-
-        float gx = -INFINITY;
-        uint32_t gid = 0xFFFFFFFFu;
-        for (int c = 0; c < g.nchunks; ++c) {
-            if (og == grp) {
-                if (!mb_wait_warp(&sh.full[s], ph, a, sh)) return;
-                const unsigned char *pb = pbase(s);
-                const int nbw = part_bytes(c);
-                const uint32_t id_lane = part_id(c);
-                float lm_unused = 0.0f;
-                uint32_t lid_unused = 0u;
-                uint32_t cm;
-                if (MODE == kGreedy) {
-                    const float b = gx;  // the penalty only lowers values
-                    cm = part_scan<T, false>(pb, nbw, id_lane, v.hs, false, [&](float m) { return m >= b; }, lm_unused,
-                                             lid_unused);
-                } else if (MODE == kTopK) {
-                    const unsigned long long te = *(volatile unsigned long long *)&st.tsh;
-                    const float b = (uint32_t)(te >> 32) == 0u ? -INFINITY : key_float((uint32_t)(te >> 32));
-                    cm = part_scan<T, false>(pb, nbw, id_lane, v.hs, false, [&](float m) { return m >= b; }, lm_unused,
-                                             lid_unused);
-                } else {
-                    const float M = key_float(*(volatile uint32_t *)&st.maxkey);
-                    const float it = a.inv_t;
-                    cm = part_scan<T, false>(pb, nbw, id_lane, v.hs, false,
-                                             [&](float m) { return m == m && scaled_diff(m, M, it) > -15.0f; },
-                                             lm_unused, lid_unused);
-                }
-                /* one candidate piece per lane per round, re-read from the
-                 * stage, penalised and tested by its lane */
-                while (__any_sync(kFull, cm != 0u)) {
-                    if (cm) {
-                        const int p = __ffs(cm) - 1;
-                        cm &= cm - 1u;
-                        const uint32_t id0 = id_lane + (uint32_t)(p * 32 * PE);
-                        float x[PE];
-                        piece_unpack<T>(*reinterpret_cast<const uint4 *>(pb + (p * 32 + lane) * 16), x);
-                        if (a.penalty) hs_penalize<PE>(v.hs, id0, x);
-                        if (MODE == kGreedy) {
+        int c = c0;
+        for (; c < g.nchunks; c += kGroups) {
+            const uint32_t qc = q + (uint32_t)c;
+            if (!chunk_wait(qc, S, a, sh)) return;
+            const int stg = (int)(qc % (uint32_t)S);
+            const unsigned char *pb = ring + (size_t)stg * kStageBytes + (size_t)part * kPartBytes;
+            const long long rem = g.body - (long long)c * kStageBytes - (long long)part * kPartBytes;
+            const int nbw = rem <= 0 ? 0 : (int)min((long long)kPartBytes, rem);
+            const uint32_t id_lane = (uint32_t)(g.head + ((long long)c * kStageBytes + (long long)part * kPartBytes) / ES) +
+                                     (uint32_t)(lane * PE);
+            float lm_unused = 0.0f;
+            uint32_t lid_unused = 0u;
+            uint32_t cm;
+            if (MODE == kGreedy) {
+                const float bnd = gx;  // the penalty only lowers values
+                cm = part_scan<T, false>(pb, nbw, id_lane, v.hs, false, [&](float m) { return m >= bnd; }, lm_unused,
+                                         lid_unused);
+            } else if (MODE == kTopK) {
+                const float bnd = filter_bound(*(volatile unsigned long long *)&st.tsh);
+                cm = part_scan<T, false>(pb, nbw, id_lane, v.hs, false, [&](float m) { return m >= bnd; }, lm_unused,
+                                         lid_unused);
+            } else {
+                const float M = key_float(*(volatile uint32_t *)&st.maxkey);
+                const float it = a.inv_t;
+                cm = part_scan<T, false>(pb, nbw, id_lane, v.hs, false,
+                                         [&](float m) { return m == m && scaled_diff(m, M, it) > -15.0f; },
+                                         lm_unused, lid_unused);
+            }
+            /* one candidate piece per lane per round, re-read from the
+             * stage, penalised and tested by its lane */
+            while (__any_sync(kFull, cm != 0u)) {
+                if (cm) {
+                    const int p = __ffs(cm) - 1;
+                    cm &= cm - 1u;
+                    const uint32_t id0 = id_lane + (uint32_t)(p * 32 * PE);
+                    float x[PE];
+                    piece_unpack<T>(*reinterpret_cast<const uint4 *>(pb + (p * 32 + lane) * 16), x);
+                    if (a.penalty) hs_penalize<PE>(v.hs, id0, x);
+                    if (MODE == kGreedy) {
 #pragma unroll
-                            for (int e = 0; e < PE; ++e)
-                                if (x[e] > gx || (x[e] == gx && id0 + (uint32_t)e < gid)) {
-                                    gx = x[e];
-                                    gid = id0 + (uint32_t)e;
-                                }
-                        } else if (MODE == kTopK) {
-                            const unsigned long long t2 = *(volatile unsigned long long *)&st.tsh;
+                        for (int e = 0; e < PE; ++e)
+                            if (x[e] > gx || (x[e] == gx && id0 + (uint32_t)e < gid)) {
+                                gx = x[e];
+                                gid = id0 + (uint32_t)e;
+                            }
+                    } else if (MODE == kTopK) {
+                        const unsigned long long t2 = *(volatile unsigned long long *)&st.tsh;
 #pragma unroll
-                            for (int e = 0; e < PE; ++e)
-                                if (x[e] == x[e] && comp_key(ord_key(x[e]), id0 + (uint32_t)e) > t2)
-                                    row_append(st, v, x[e], id0 + (uint32_t)e);
-                        } else {
-                            float m = -INFINITY;
+                        for (int e = 0; e < PE; ++e)
+                            if (x[e] == x[e] && comp_key(ord_key(x[e]), id0 + (uint32_t)e) > t2)
+                                row_append(st, v, x[e], id0 + (uint32_t)e);
+                    } else {
+                        float m = -INFINITY;
 #pragma unroll
-                            for (int e = 0; e < PE; ++e) m = fmaxf(m, x[e]);
-                            if (m > -INFINITY) atomicMax(&st.maxkey, ord_key(m));
-                            const float M = key_float(*(volatile uint32_t *)&st.maxkey);
+                        for (int e = 0; e < PE; ++e) m = fmaxf(m, x[e]);
+                        if (m > -INFINITY) atomicMax(&st.maxkey, ord_key(m));
+                        const float M = key_float(*(volatile uint32_t *)&st.maxkey);
 #pragma unroll
-                            for (int e = 0; e < PE; ++e)
-                                if (scaled_diff(x[e], M, a.inv_t) > -15.0f) row_append(st, v, x[e], id0 + (uint32_t)e);
-                        }
+                        for (int e = 0; e < PE; ++e)
+                            if (scaled_diff(x[e], M, a.inv_t) > -15.0f) row_append(st, v, x[e], id0 + (uint32_t)e);
                     }
                 }
-                __syncwarp();
-                if (lane == 0) mb_arrive(&sh.empty[s]);
             }
-            if (++s == S) {
-                s = 0;
-                ph ^= 1u;
-            }
-            if (++og == kGroups) og = 0;
+            __syncwarp();
+            if (lane == 0) mb_arrive(&sh.empty[stg]);
         }
+        q += (uint32_t)g.nchunks;
         if (MODE == kGreedy) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -1037,13 +1118,14 @@ __global__ void __launch_bounds__(kSThreads, 1) stream_rows_kernel(const __grid_
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mb_init(&sh.full[s], 1);
-            mb_init(&sh.empty[s], kParts);  // released by the stage's group of consumer warps
+            mb_init(&sh.empty[s], kParts);  // released by the chunk's group of consumer warps
         }
         for (int f = 0; f < kSFin; ++f) {
             mb_init(&sh.ready[f], 1);
             mb_init(&sh.done[f], kSCons);
-            mb_init(&sh.warm[f], kSCons);
         }
+        for (int g = 0; g < kGroups; ++g) mb_init(&sh.gmeet[g], kParts);
+        sh.issued = 0u;
         sh.err = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1053,9 +1135,7 @@ __global__ void __launch_bounds__(kSThreads, 1) stream_rows_kernel(const __grid_
         /* ---- producer ---- */
         if (lane != 0 || a.test_stall) return;
         const uint64_t pol = l2_evict_first();
-        long long issued = 0;
-        int s = 0;
-        uint32_t ph = 0u;  // phase parity of stage s's next fill
+        uint32_t q = 0u;  // chunks issued
         bool alive = true;
         for (int row = blockIdx.x; row < a.batch && alive; row += G) {
             const RowSpan span = row_span(a, row);
@@ -1063,29 +1143,27 @@ __global__ void __launch_bounds__(kSThreads, 1) stream_rows_kernel(const __grid_
             const BulkGeom g = bulk_geom<T>(rowp, span.V);
             const char *src = rowp + (size_t)g.head * F::ES;
             long long left = g.body;
-            for (int c = 0; c < g.nchunks; ++c) {
-                /* the consumers released this stage's previous fill (none on the first lap) */
-                if (issued >= S && !mb_try(&sh.empty[s], ph ^ 1u) && !mb_wait_thread(&sh.empty[s], ph ^ 1u, a, sh)) {
+            for (int c = 0; c < g.nchunks; ++c, ++q) {
+                const int s = (int)(q % (uint32_t)S);
+                const uint32_t fill = q / (uint32_t)S;
+                /* the consumers released the stage's previous fill (none on the first lap) */
+                if (fill > 0u && !mb_try(&sh.empty[s], (fill - 1u) & 1u) &&
+                    !mb_wait_thread(&sh.empty[s], (fill - 1u) & 1u, a, sh)) {
                     alive = false;
                     break;
                 }
                 const uint32_t nb = left < kStageBytes ? (uint32_t)left : (uint32_t)kStageBytes;
                 mb_expect_tx(&sh.full[s], nb);
                 bulk_load(stream_smem + (size_t)s * kStageBytes, src, nb, &sh.full[s], pol);
+                st_release_shared(&sh.issued, q + 1u);
                 src += nb;
                 left -= nb;
-                ++issued;
-                if (++s == S) {
-                    s = 0;
-                    ph ^= 1u;
-                }
             }
         }
         /* copies still in flight land before the CTA may leave: the last
-         * fill of each stage (stage s's last fill had parity ph ^ 1 when it
-         * wrapped, ph otherwise) */
-        for (int i = 0; i < S && i < issued; ++i) {
-            const uint32_t par = i < s ? ph : (ph ^ 1u);
+         * fill of each stage */
+        for (uint32_t i = 0; i < (uint32_t)S && i < q; ++i) {
+            const uint32_t par = ((q - 1u - i) / (uint32_t)S) & 1u;
             if (!mb_try(&sh.full[i], par)) {
                 const uint64_t t0 = gtimer();
                 while (!mb_try(&sh.full[i], par))
@@ -1102,10 +1180,11 @@ __global__ void __launch_bounds__(kSThreads, 1) stream_rows_kernel(const __grid_
         return;
     }
 
-    /* ---- finisher f: rows j = f, f + 2, ... of this CTA ---- */
+    /* ---- finisher f: rows j = f, f + kSFin, ... of this CTA ---- */
     const int f = warp - 1 - kSCons;
     const SetView v = set_view(stream_smem, L, a, f);
     unsigned char *fin = stream_smem + L.ring + (size_t)kSFin * L.set_bytes + (size_t)f * L.fin_bytes;
+    uint32_t *hist = reinterpret_cast<uint32_t *>(fin + L.rh);
     StreamRow &st = sh.st[f];
     int j = f;
     int row = blockIdx.x + j * G;
@@ -1114,9 +1193,9 @@ __global__ void __launch_bounds__(kSThreads, 1) stream_rows_kernel(const __grid_
         if (lane == 0) mb_arrive(&sh.ready[f]);
     }
     for (; row < a.batch; j += kSFin, row += kSFin * G) {
-        const uint32_t par = (uint32_t)(j >> 1) & 1u;
+        const uint32_t par = (uint32_t)(j / kSFin) & 1u;
         if (MODE == kTopK) {
-            if (!stream_maintain(a, sh, st, v, reinterpret_cast<uint32_t *>(fin + L.rh), &sh.done[f], par)) return;
+            if (!stream_maintain(a, sh, st, v, hist, &sh.done[f], par)) return;
         } else if (!mb_wait_warp(&sh.done[f], par, a, sh)) {
             return;
         }
