@@ -519,7 +519,7 @@ def run_vocab_sharded(args):
             "cpu_baseline": None,
             "e2e": {"value": B * e2e_steps / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": B * width * 4,
                     "d2h_bytes_per_step": B * 4, "steps": e2e_steps,
-                    "api": "noel_b200.sharded (select, NCCL all-gather, merge) from pinned host shards"},
+                    "api": "noel_b200.sharded (select, NCCL all-to-all of row blocks, merge, NCCL all-gather of results) from pinned host shards"},
             "rows_from_full_rows": n_full[0],
             "clocks": clk,
             "gpu_launches": 3 * args.steps,

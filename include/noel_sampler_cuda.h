@@ -111,33 +111,40 @@ int noel_sampler_sample_batch_noalloc(const noel_sampler_config_t *cfg, const vo
  * which samples whole rows on the host (sampler.c:80-192); the result equals
  * noel_sampler_sample on the full row.  Three steps:
  *
- *   1. noel_sampler_shard_select on every GPU: for each of the batch rows, the
- *      shard's K best (global id, penalised logit) by (logit desc, id asc),
- *      K = noel_sampler_shard_kprime(cfg); its largest penalised logit; flags.
- *   2. an all-gather of entries [B][K][2] u32, maxima [B] f32 and flags [B]
- *      i32 across the ranks, in rank order (e.g. ncclAllGather).
- *   3. noel_sampler_shard_merge on every GPU (identical results everywhere):
- *      the row's sample from the gathered lists.  A row whose top-k boundary
- *      cannot be decided from them (a weight tie reaching below the gathered
- *      entries) gets status 1 and keeps its RNG state: sample it from its full
- *      row (gather the row's shards) with noel_sampler_sample_batch.
+ *   1. noel_sampler_shard_select on every GPU: per row, a list of
+ *      L = noel_sampler_shard_list_len(cfg) entries (global id, penalised
+ *      logit bits) by (logit desc, id asc), id -1 past the listed ones, then a
+ *      trailer (largest penalised logit bits, flags): d_lists [B][L + 1][2]
+ *      u32.  Greedy lists the shard's best element; top-k (k <= 120) its best
+ *      k + 8; top-k off or above 120 its elements within the -15 cut under
+ *      its own maximum (at most 256).
+ *   2. an exchange that gives the rank merging rows [r0, r1) every shard's
+ *      lists of those rows, shard-major: [n_shards][r1 - r0][L + 1][2]
+ *      (an all-to-all of contiguous row blocks, or an all-gather of
+ *      everything).
+ *   3. noel_sampler_shard_merge: the rows' samples from those lists, with
+ *      their RNG states d_rng [rows][2] (in/out).  A row that cannot be
+ *      decided from them (a weight tie at the top-k boundary reaching below
+ *      the gathered entries, or a full-list shard that left out elements
+ *      within the row's cut) gets status 1 and keeps its RNG state: sample it
+ *      from its full row (gather the row's shards) with
+ *      noel_sampler_sample_batch.
  *
- * Supported configs: greedy (temperature <= 1e-4) or 0 < top_k <= 120; others
- * return NOEL_ERR_UNSUPPORTED (they need every candidate of the row).  The
- * penalty applies to the history ids inside the shard; d_history holds global
- * ids.  d_logits points at the shard's first column; ld is its row stride.
+ * The penalty applies to the history ids inside the shard; d_history holds
+ * global ids.  d_logits points at the shard's first column; ld is its row
+ * stride.  A full-list shard whose history table and list do not fit the
+ * streaming kernel's shared memory returns NOEL_ERR_UNSUPPORTED.
  */
-int noel_sampler_shard_kprime(const noel_sampler_config_t *cfg);
+int noel_sampler_shard_list_len(const noel_sampler_config_t *cfg);
 int noel_sampler_shard_select(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
                               int batch, int shard_vocab, size_t ld, int v_begin,
                               const int32_t *d_history, int history_len, size_t hld,
-                              uint32_t *d_entries, float *d_max, int32_t *d_flags, void *stream);
-/* d_entries [n_shards][B][K][2], d_max [n_shards][B], d_flags [n_shards][B];
- * d_rng [B][2] in/out, d_ids [B], d_probs [B] or NULL, d_status [B]. */
+                              uint32_t *d_lists, void *stream);
+/* d_lists [n_shards][batch][L + 1][2]; d_rng [batch][2] in/out, d_ids [batch],
+ * d_probs [batch] or NULL, d_status [batch]. */
 int noel_sampler_shard_merge(const noel_sampler_config_t *cfg, int n_shards, int batch,
-                             const uint32_t *d_entries, const float *d_max, const int32_t *d_flags,
-                             uint64_t *d_rng, int32_t *d_ids, float *d_probs, int32_t *d_status,
-                             void *stream);
+                             const uint32_t *d_lists, uint64_t *d_rng, int32_t *d_ids, float *d_probs,
+                             int32_t *d_status, void *stream);
 
 /*
  * Host-buffer form of noel_sampler_sample_batch for callers whose logits are

@@ -186,8 +186,8 @@ constexpr int kWarpKprimeMax = 128;  // warp-streaming kernel up to k = 120
 constexpr int kCapMax = 4096;
 
 template <typename T>
-int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, bool stream, size_t smem_main,
-             size_t smem_exact, DeviceCtx *c, cudaStream_t s) {
+int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, bool stream, bool exact_only,
+             size_t smem_main, size_t smem_exact, DeviceCtx *c, cudaStream_t s) {
     const void *kmain = nullptr;
     if (stream) kmain = mode == kGreedy ? (const void *)stream_rows_kernel<T, kGreedy>
                         : mode == kTopK ? (const void *)stream_rows_kernel<T, kTopK>
@@ -199,14 +199,16 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, bool 
     else kmain = wide ? (const void *)sample_rows_kernel<T, kFullList, 4>
                       : (const void *)sample_rows_kernel<T, kFullList, 1>;
     const void *kexact = (const void *)exact_rows_kernel<T>;
-    int r = set_smem(c, kmain, smem_main);
+    int r = exact_only ? NOEL_OK : set_smem(c, kmain, smem_main);
     if (r) return r;
     r = set_smem(c, kexact, smem_exact);
     if (r) return r;
     if (t_ev_before) CUDA_TRY(cudaEventRecord(t_ev_before, s));
     const int grid = a0.batch;  // one CTA per row (the streaming kernel: one per SM, rows in turn)
     const int sgrid = a0.batch < c->sms ? a0.batch : c->sms;
-    if (stream && mode == kGreedy) stream_rows_kernel<T, kGreedy><<<sgrid, kSThreads, smem_main, s>>>(a0);
+    if (exact_only) list_all_rows_kernel<<<(a0.batch + 255) / 256 < c->sms ? (a0.batch + 255) / 256 : c->sms, 256, 0,
+                                            s>>>(a0);
+    else if (stream && mode == kGreedy) stream_rows_kernel<T, kGreedy><<<sgrid, kSThreads, smem_main, s>>>(a0);
     else if (stream && mode == kTopK) stream_rows_kernel<T, kTopK><<<sgrid, kSThreads, smem_main, s>>>(a0);
     else if (stream) stream_rows_kernel<T, kFullList><<<sgrid, kSThreads, smem_main, s>>>(a0);
     else if (block_kernel) sample_rows_block_kernel<T, kTopK><<<grid, kMainThreads, smem_main, s>>>(a0);
@@ -240,9 +242,7 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, bool 
 /* vocab shard output of sample_batch (see SampleArgs) */
 struct ShardOut {
     int id_off;
-    uint2 *entries;
-    float *maxes;
-    int32_t *flags;
+    uint2 *lists;
     int split = 0, split_vocab = 0;  // row splitting (see SampleArgs)
 };
 
@@ -261,12 +261,18 @@ int warp_keep(int kprime) { return kprime <= 32 ? kprime : (kprime <= 64 ? 3 * k
  * large one rarely; 128 entries measured best for K' = 16, 64 and 128. */
 int warp_buffer(int kw) { return 2 * kw > 128 ? 2 * kw : 128; }
 
-/* entries per row and shard for a config: K' of top-k, 16 for greedy; 0 when
- * the config needs every candidate (top-k off or above 120) */
-int shard_kprime(const noel_sampler_config_t *cfg) {
-    if (cfg->temperature <= 1e-4f) return 16;
-    if (cfg->top_k <= 0 || cfg->top_k > kWarpKprimeMax - 8) return 0;
-    return pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
+/* How a config is vocab-sharded: greedy lists each shard's best element
+ * (selected among its 16 best); top-k with k <= 120 its best k + 8 (selected
+ * among its K' = pow2(k + 8) best); top-k off or above 120 every element
+ * within the -15 cut under its own maximum, up to kShardFullLen of them. */
+struct ShardPlan {
+    int mode, kprime, len;
+};
+ShardPlan shard_plan(const noel_sampler_config_t *cfg) {
+    if (cfg->temperature <= 1e-4f) return {kTopK, 16, 1};  // sampler.c:106
+    if (cfg->top_k > 0 && cfg->top_k <= kWarpKprimeMax - 8)
+        return {kTopK, pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16), cfg->top_k + 8};
+    return {kFullList, 0, kShardFullLen};
 }
 
 /* B rows of V columns, one CTA per row (or per range of a row, with a shard
@@ -279,8 +285,8 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     if (B < 0 || V <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", B, V);
     if (B == 0) return ok();
     if (!logits || (!so && (!rng || !ids))) return fail(NOEL_ERR_INVALID_ARG, "logits, rng and ids are required");
-    if (so && (!so->entries || !so->maxes || !so->flags || so->id_off < 0))
-        return fail(NOEL_ERR_INVALID_ARG, "shard entries, maxima and flags are required, v_begin >= 0");
+    if (so && (!so->lists || so->id_off < 0))
+        return fail(NOEL_ERR_INVALID_ARG, "shard lists are required, v_begin >= 0");
     if (dtype != NOEL_DTYPE_F32 && dtype != NOEL_DTYPE_BF16) return fail(NOEL_ERR_INVALID_ARG, "dtype %d", dtype);
     if (ld < (size_t)V) return fail(NOEL_ERR_INVALID_ARG, "ld %zu < vocab %d", ld, V);
     const int es = dtype == NOEL_DTYPE_F32 ? 4 : 2;
@@ -329,23 +335,25 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     a.et = c->et;
 
     int mode;
-    if (so) mode = kTopK;            // a vocab shard lists its K' best in every mode
+    const ShardPlan sp = so ? shard_plan(cfg) : ShardPlan{0, 0, 0};
+    if (so) mode = sp.mode;          // a vocab shard lists its best elements
     else if (T <= 1e-4f) mode = kGreedy;  // sampler.c:106
     else if (cfg->top_k > 0 && cfg->top_k <= kMaxKprime - 8) mode = kTopK;
     else mode = kFullList;
     bool block_kernel = false;
     if (so) {
-        a.kprime = shard_kprime(cfg);
-        if (!a.kprime)
-            return fail(NOEL_ERR_UNSUPPORTED, "a vocab shard needs greedy or 0 < top_k <= %d", kWarpKprimeMax - 8);
         a.id_off = so->id_off;
-        a.shard_entries = so->entries;
-        a.shard_max = so->maxes;
-        a.shard_flags = so->flags;
+        a.shard_lists = so->lists;
+        a.shard_len = sp.len;
         a.split = so->split;
         a.split_vocab = so->split_vocab;
-        a.kw = warp_keep(a.kprime);
-        a.cap = warp_buffer(a.kw);
+        if (mode == kTopK) {
+            a.kprime = sp.kprime;
+            a.kw = warp_keep(a.kprime);
+            a.cap = warp_buffer(a.kw);
+        } else {
+            a.cap = 256;
+        }
     } else if (mode == kTopK) {
         a.kprime = pow2_at_least(cfg->top_k + 8 > 16 ? cfg->top_k + 8 : 16);
         if (a.kprime <= kWarpKprimeMax) {
@@ -393,7 +401,10 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
             a.hcap = 0;
         }
     }
-    if (stream) {
+    /* a full-list vocab shard whose history table and list do not fit the
+     * streaming kernel: every row goes to the two-pass kernel */
+    const bool exact_only = so && mode == kFullList && !stream;
+    if (stream || exact_only) {
     } else if (block_kernel) {
         /* the block kernel's history also holds the id of each rank while
          * it computes the penalised values */
@@ -443,8 +454,9 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
         a.slots = w->slots;
         a.nslots = w->nslots;
     }
-    r = dtype == NOEL_DTYPE_F32 ? launch_t<float>(a, mode, block_kernel, wide, stream, smem_main, smem_exact, c, s)
-                                : launch_t<uint16_t>(a, mode, block_kernel, wide, stream, smem_main, smem_exact, c, s);
+    r = dtype == NOEL_DTYPE_F32
+            ? launch_t<float>(a, mode, block_kernel, wide, stream, exact_only, smem_main, smem_exact, c, s)
+            : launch_t<uint16_t>(a, mode, block_kernel, wide, stream, exact_only, smem_main, smem_exact, c, s);
     if (r) return r;
     return ok();
 }
@@ -758,33 +770,32 @@ thread_local HostBatchStage t_hb;
 }  // namespace
 
 /* ------------------------------------------------------ vocab-sharded rows */
-extern "C" int noel_sampler_shard_kprime(const noel_sampler_config_t *cfg) {
+extern "C" int noel_sampler_shard_list_len(const noel_sampler_config_t *cfg) {
     if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
-    return shard_kprime(cfg);
+    return shard_plan(cfg).len;
 }
 
 extern "C" int noel_sampler_shard_select(const noel_sampler_config_t *cfg, const void *d_logits, int dtype,
                                          int batch, int shard_vocab, size_t ld, int v_begin,
                                          const int32_t *d_history, int history_len, size_t hld,
-                                         uint32_t *d_entries, float *d_max, int32_t *d_flags, void *stream) {
-    ShardOut so{v_begin, reinterpret_cast<uint2 *>(d_entries), d_max, d_flags};
-    if (reinterpret_cast<uintptr_t>(d_entries) & 7) return fail(NOEL_ERR_INVALID_ARG, "d_entries must be 8-byte aligned");
+                                         uint32_t *d_lists, void *stream) {
+    ShardOut so{v_begin, reinterpret_cast<uint2 *>(d_lists)};
+    if (reinterpret_cast<uintptr_t>(d_lists) & 7) return fail(NOEL_ERR_INVALID_ARG, "d_lists must be 8-byte aligned");
     return sample_batch(cfg, d_logits, dtype, batch, shard_vocab, ld, d_history, history_len, hld, nullptr, nullptr,
                         nullptr, static_cast<cudaStream_t>(stream), nullptr, &so);
 }
 
 extern "C" int noel_sampler_shard_merge(const noel_sampler_config_t *cfg, int n_shards, int batch,
-                                        const uint32_t *d_entries, const float *d_max, const int32_t *d_flags,
-                                        uint64_t *d_rng, int32_t *d_ids, float *d_probs, int32_t *d_status,
-                                        void *stream) {
+                                        const uint32_t *d_lists, uint64_t *d_rng, int32_t *d_ids, float *d_probs,
+                                        int32_t *d_status, void *stream) {
     if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
     if (n_shards <= 0 || batch < 0) return fail(NOEL_ERR_INVALID_ARG, "n_shards %d / batch %d", n_shards, batch);
     if (batch == 0) return ok();
-    const int K = shard_kprime(cfg);
-    if (!K) return fail(NOEL_ERR_UNSUPPORTED, "a vocab shard needs greedy or 0 < top_k <= %d", kWarpKprimeMax - 8);
-    if (!d_entries || !d_max || !d_flags || !d_rng || !d_ids || !d_status)
-        return fail(NOEL_ERR_INVALID_ARG, "entries, maxima, flags, rng, ids and status are required");
-    if (reinterpret_cast<uintptr_t>(d_entries) & 7) return fail(NOEL_ERR_INVALID_ARG, "d_entries must be 8-byte aligned");
+    const ShardPlan sp = shard_plan(cfg);
+    const int K = sp.len;
+    if (!d_lists || !d_rng || !d_ids || !d_status)
+        return fail(NOEL_ERR_INVALID_ARG, "lists, rng, ids and status are required");
+    if (reinterpret_cast<uintptr_t>(d_lists) & 7) return fail(NOEL_ERR_INVALID_ARG, "d_lists must be 8-byte aligned");
     DeviceCtx *c = nullptr;
     int r = device_ctx(&c);
     if (r) return r;
@@ -796,12 +807,9 @@ extern "C" int noel_sampler_shard_merge(const noel_sampler_config_t *cfg, int n_
     MergeArgs m{};
     m.n_shards = n_shards;
     m.batch = batch;
-    m.kprime = K;
-    m.es = batch;  // [n_shards][batch] lists, as gathered across ranks
-    m.eb = 1;
-    m.entries = reinterpret_cast<const uint2 *>(d_entries);
-    m.maxes = d_max;
-    m.flags = d_flags;
+    m.len = K;
+    m.full = sp.mode == kFullList;
+    m.lists = reinterpret_cast<const uint2 *>(d_lists);
     m.greedy = cfg->temperature <= 1e-4f;  // sampler.c:106
     m.inv_t = 1.0f / cfg->temperature;     // sampler.c:132
     m.top_p = cfg->top_p;

@@ -79,12 +79,13 @@ struct SampleArgs {
     ExpTable et;
     /* vocab shard (the row holds columns [id_off, id_off + vocab) of the full
      * vocabulary): history ids are global; instead of sampling, the kernels
-     * write the shard's kprime best (global id, penalised logit) by (logit
-     * desc, id asc), its largest penalised logit and flags */
+     * write per row the shard's best shard_len (global id, penalised logit)
+     * by (logit desc, id asc) -- for a full-list config only elements within
+     * the -15 cut under the shard's maximum -- and then a trailer (largest
+     * penalised logit, flags) */
     int id_off;
-    uint2 *shard_entries;       // [B][kprime], id -1 past the listed ones; NULL: no shard output
-    float *shard_max;           // [B] -inf when the shard holds no number
-    int32_t *shard_flags;       // [B] kShardNaN0 | kShardMore
+    uint2 *shard_lists;         // [B][shard_len + 1], id -1 past the listed ones; NULL: no shard output
+    int shard_len;
     /* split rows (with shard output): kernel row r is columns
      * [s * vocab, s * vocab + vocab) of caller row r / split, s = r % split,
      * of a row of split_vocab columns; 0 or 1: rows are the caller's rows */
@@ -122,6 +123,7 @@ __device__ __forceinline__ RowSpan row_span(const SampleArgs &a, int r) {
 /* shard flags */
 enum { kShardNaN0 = 1, kShardMore = 2 };
 
+
 /* ---------------------------------------------------------------------- */
 /* scalar helpers                                                          */
 
@@ -134,6 +136,24 @@ __device__ __forceinline__ float key_float(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 constexpr uint32_t kKeyNegInf = 0x007FFFFFu;   // ord_key(-inf)
+
+/* One row's shard list: m listed entries from get(i) -> (local id, key),
+ * padding, then the trailer.  By the calling warp. */
+template <typename Get>
+__device__ __forceinline__ void shard_write(const SampleArgs &a, int row, int id_off, int m, float mx, int flags,
+                                            Get get) {
+    const int lane = threadIdx.x & 31;
+    uint2 *out = a.shard_lists + (size_t)row * (size_t)(a.shard_len + 1);
+    for (int i = lane; i < a.shard_len; i += 32) {
+        uint2 e = make_uint2(0xFFFFFFFFu, 0u);
+        if (i < m) {
+            const uint2 ik = get(i);
+            e = make_uint2(ik.x + (uint32_t)id_off, __float_as_uint(key_float(ik.y)));
+        }
+        out[i] = e;
+    }
+    if (lane == 0) out[a.shard_len] = make_uint2(__float_as_uint(mx), (uint32_t)flags);
+}
 
 /* sampler.c:96-100 applied c times (one per occurrence in the window) */
 __device__ __forceinline__ float apply_penalty(float x, uint32_t c, float rep) {

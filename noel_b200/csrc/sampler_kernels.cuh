@@ -49,6 +49,13 @@ __device__ __forceinline__ void list_exact_row(const SampleArgs &a, int row) {
     a.exact_list[q] = row;
 }
 
+/* Every row of the launch for exact_rows_kernel (the rows of a full-list
+ * vocab shard whose history and list do not fit the streaming kernel). */
+__global__ void list_all_rows_kernel(const SampleArgs a) {
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < a.batch; r += gridDim.x * blockDim.x) a.exact_list[r] = r;
+    if (blockIdx.x == 0 && threadIdx.x == 0) a.counters[0] = a.batch;
+}
+
 /* ====================================================================== */
 /* block-level kernel for large kept sets (k > 120): one CTA per row       */
 
@@ -676,7 +683,7 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
                 wb[e] = 0u;
                 if (i < Vr) {
                     const float x = load(i);
-                    if (a.shard_entries) {
+                    if (a.shard_lists) {
                         /* a vocab shard lists every number by logit (greedy
                          * rows need them all; ord_key is never 0) */
                         if (x == x) {
@@ -703,16 +710,13 @@ __global__ void __launch_bounds__(kExactThreads) exact_rows_kernel(const SampleA
         const bool fb = n == 0;
         uint2 *sorted = slotA;
         if (n > 1) sorted = radix_sort_stable<NT>(slotA, slotB, n, s_h, s_w, &s_skip);
-        if (a.shard_entries) {
-            /* vocab shard: its K' best by (logit desc, id asc) */
-            const int m = min(n, a.kprime);
-            uint2 *out = a.shard_entries + (size_t)row * a.kprime;
-            for (int i = tid; i < a.kprime; i += NT)
-                out[i] = i < m ? make_uint2(sorted[i].y + (uint32_t)span.id_off, __float_as_uint(key_float(~sorted[i].x)))
-                               : make_uint2(0xFFFFFFFFu, 0u);
-            if (tid == 0) {
-                a.shard_max[row] = key_float(mk);
-                a.shard_flags[row] = (s_l0nan ? kShardNaN0 : 0) | (n > a.kprime ? kShardMore : 0);
+        if (a.shard_lists) {
+            /* vocab shard: its best shard_len by (logit desc, id asc) */
+            if (tid < 32) {
+                const int m = min(n, a.shard_len);
+                shard_write(a, row, span.id_off, m, n > 0 ? key_float(mk) : -INFINITY,
+                            (s_l0nan ? kShardNaN0 : 0) | (n > m ? kShardMore : 0),
+                            [&](int i) { return make_uint2(sorted[i].y, ~sorted[i].x); });
             }
             __syncthreads();
             continue;

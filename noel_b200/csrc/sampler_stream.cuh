@@ -766,7 +766,9 @@ __device__ __noinline__ void stream_finish(const SampleArgs &a, const StreamRow 
     }
     if (MODE == kFullList) {
         /* the candidates: entries within the -15 cut under the row maximum */
-        const float Mfull = st.l0nan ? __uint_as_float(0x7FC00000u) : key_float(st.maxkey);
+        /* NaN at the row's id 0 (for a vocab shard: at global id 0 only) */
+        const bool nan0 = st.l0nan && span.id_off == 0;
+        const float Mfull = nan0 ? __uint_as_float(0x7FC00000u) : key_float(st.maxkey);
         const int n = buf_compact(gk, gi, cnt, [&](uint32_t k, uint32_t) {
             return scaled_diff(key_float(k), Mfull, a.inv_t) > -15.0f;
         });
@@ -776,6 +778,22 @@ __device__ __noinline__ void stream_finish(const SampleArgs &a, const StreamRow 
             return;
         }
         const int Pn = stream_pow2(max(n, 1));
+        if (a.shard_lists) {
+            /* vocab shard: its candidates under its own maximum (a superset
+             * of its elements within the cut under the row's maximum) by
+             * (logit desc, id asc), at most shard_len of them */
+            for (int i = lane; i < Pn; i += 32) sk[i] = i < n ? comp_key(gk[i], gi[i]) : 0ull;
+            __syncwarp();
+            if (n > 1) warp_bitonic_desc(sk, Pn);
+            __syncwarp();
+            const int m = min(n, a.shard_len);
+            const uint32_t mk = *(volatile uint32_t *)&st.maxkey;
+            shard_write(a, row, span.id_off, m, nan0 ? __uint_as_float(0x7FC00000u) : key_float(mk),
+                        (nan0 ? kShardNaN0 : 0) | (n > m ? kShardMore : 0),
+                        [&](int i) { return make_uint2(0xFFFFFFFFu - (uint32_t)sk[i], (uint32_t)(sk[i] >> 32)); });
+            __syncwarp();
+            return;
+        }
         for (int i = lane; i < Pn; i += 32) {
             uint64_t kv = 0ull;
             if (i < n) {
@@ -819,18 +837,14 @@ __device__ __noinline__ void stream_finish(const SampleArgs &a, const StreamRow 
         n = a.kprime;
         trunc = true;
     }
-    if (a.shard_entries) {
-        /* vocab shard: its K' best by (logit desc, id asc), its largest
-         * penalised logit, and whether it holds more elements than listed */
-        const int m = min(n, a.kprime);
-        uint2 *out = a.shard_entries + (size_t)row * a.kprime;
-        for (int i = lane; i < a.kprime; i += 32)
-            out[i] = i < m ? make_uint2(gi[i] + (uint32_t)span.id_off, __float_as_uint(key_float(gk[i])))
-                           : make_uint2(0xFFFFFFFFu, 0u);
-        if (lane == 0) {
-            a.shard_max[row] = m > 0 ? key_float(gk[0]) : -INFINITY;
-            a.shard_flags[row] = (st.l0nan && span.id_off == 0 ? kShardNaN0 : 0) | (trunc ? kShardMore : 0);
-        }
+    if (a.shard_lists) {
+        /* vocab shard: its best shard_len by (logit desc, id asc), its
+         * largest penalised logit, and whether it holds more elements than
+         * listed */
+        const int m = min(n, a.shard_len);
+        shard_write(a, row, span.id_off, m, n > 0 ? key_float(gk[0]) : -INFINITY,
+                    (st.l0nan && span.id_off == 0 ? kShardNaN0 : 0) | (trunc || n > m ? kShardMore : 0),
+                    [&](int i) { return make_uint2(gi[i], gk[i]); });
         __syncwarp();
         return;
     }

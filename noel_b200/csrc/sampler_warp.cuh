@@ -763,20 +763,16 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
         n = a.kprime;
         trunc = true;
     }
-    if (MODE == kTopK && a.shard_entries) {
-        /* vocab shard: its K' best by (logit desc, id asc), its largest
-         * penalised logit, and whether it holds more elements than listed */
+    if (MODE == kTopK && a.shard_lists) {
+        /* vocab shard: its best shard_len of its K' best by (logit desc, id
+         * asc), its largest penalised logit, and whether it holds more
+         * elements than listed */
         if (!trunc && !bsort) warp_topk_sorted_r<4>(L.ukey, L.uid, n, a.kprime, nullptr, 1);
-        const int m = min(n, a.kprime);
+        const int m = min(n, a.shard_len);
         const int id_off = row_span(a, row).id_off;
-        uint2 *out = a.shard_entries + (size_t)row * a.kprime;
-        for (int i = lane; i < a.kprime; i += 32)
-            out[i] = i < m ? make_uint2(L.uid[i] + (uint32_t)id_off, __float_as_uint(key_float(L.ukey[i])))
-                           : make_uint2(0xFFFFFFFFu, 0u);
-        if (lane == 0) {
-            a.shard_max[row] = m > 0 ? key_float(L.ukey[0]) : -INFINITY;
-            a.shard_flags[row] = (rs.l0nan && id_off == 0 ? kShardNaN0 : 0) | (trunc ? kShardMore : 0);
-        }
+        shard_write(a, row, id_off, m, n > 0 ? key_float(L.ukey[0]) : -INFINITY,
+                    (rs.l0nan && id_off == 0 ? kShardNaN0 : 0) | (trunc || n > m ? kShardMore : 0),
+                    [&](int i) { return make_uint2(L.uid[i], L.ukey[i]); });
         return;
     }
     float M = Mfull;

@@ -103,17 +103,17 @@ def lib() -> C.CDLL:
         C.POINTER(SamplerConfig), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_void_p,
         C.c_int, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p,
     ]
-    L.noel_sampler_shard_kprime.restype = C.c_int
-    L.noel_sampler_shard_kprime.argtypes = [C.POINTER(SamplerConfig)]
+    L.noel_sampler_shard_list_len.restype = C.c_int
+    L.noel_sampler_shard_list_len.argtypes = [C.POINTER(SamplerConfig)]
     L.noel_sampler_shard_select.restype = C.c_int
     L.noel_sampler_shard_select.argtypes = [
         C.POINTER(SamplerConfig), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_size_t, C.c_int,
-        C.c_void_p, C.c_int, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+        C.c_void_p, C.c_int, C.c_size_t, C.c_void_p, C.c_void_p,
     ]
     L.noel_sampler_shard_merge.restype = C.c_int
     L.noel_sampler_shard_merge.argtypes = [
-        C.POINTER(SamplerConfig), C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
-        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+        C.POINTER(SamplerConfig), C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+        C.c_void_p, C.c_void_p,
     ]
     L.noel_sampler_cuda_last_error.restype = C.c_int
     L.noel_sampler_cuda_last_error_message.restype = C.c_char_p

@@ -5,17 +5,22 @@ src/sampler.c:80-192).  When a row's logits are produced by a vocab-parallel
 LM head, each GPU holds only its columns; this module samples such rows
 without moving them:
 
-  1. ``noel_sampler_shard_select`` on every rank: per row, the shard's K best
-     (global id, penalised logit), its largest penalised logit and flags;
-  2. one all-gather (NCCL over NVLink) of those lists, in rank order;
-  3. ``noel_sampler_shard_merge`` on every rank (identical results): the
-     row's sample, equal to the reference's on the full row;
-  4. the rare rows the merge cannot decide (a weight tie at the top-k boundary
-     reaching below the gathered entries) are gathered whole and sampled by
-     ``noel_sampler_sample_batch``.
+  1. ``noel_sampler_shard_select`` on every rank: per row, a list of the
+     shard's best entries (global id, penalised logit) and a trailer (its
+     largest penalised logit, flags);
+  2. one all-to-all (NCCL over NVLink): rank r receives every shard's lists
+     of its block of rows;
+  3. ``noel_sampler_shard_merge`` on every rank, for its block of rows only;
+  4. one all-gather of the blocks' results (ids, status, RNG states and
+     optionally probabilities), so every rank holds every row's result and the
+     replicated RNG states stay identical;
+  5. the rare rows the merge cannot decide (a weight tie at the top-k boundary
+     reaching below the gathered entries, or a full-list shard that left out
+     elements within the row's cut) are gathered whole and sampled by
+     ``noel_sampler_sample_batch`` on every rank.
 
-Every rank takes the same collective steps in the same order.  The per-row
-RNG states are replicated on every rank and advance identically.
+Every rank takes the same collective steps in the same order.  Step 5 needs
+the undecided-row count on the host: one 4-byte read per call.
 """
 from __future__ import annotations
 
@@ -27,46 +32,42 @@ from . import sampler as S
 class CudaKernels:
     """The library's kernels for each step (the product path)."""
 
-    def kprime(self, cfg) -> int:
-        return S.lib().noel_sampler_shard_kprime(C.byref(cfg))
+    def list_len(self, cfg) -> int:
+        return S.lib().noel_sampler_shard_list_len(C.byref(cfg))
 
     def select(self, cfg, logits_shard, v_begin: int, history=None):
+        """Lists [B, L + 1, 2] int32 of the shard's columns."""
         import torch
 
         assert logits_shard.is_cuda and logits_shard.dim() == 2 and logits_shard.stride(1) == 1
         B, Vs = logits_shard.shape
-        K = self.kprime(cfg)
-        if K <= 0:
-            raise S.NoelSamplerError(-3, "vocab-sharded sampling needs greedy or 0 < top_k <= 120")
-        dev = logits_shard.device
-        entries = torch.empty(B, K, 2, dtype=torch.int32, device=dev)
-        maxes = torch.empty(B, dtype=torch.float32, device=dev)
-        flags = torch.empty(B, dtype=torch.int32, device=dev)
+        L = self.list_len(cfg)
+        lists = torch.empty(B, L + 1, 2, dtype=torch.int32, device=logits_shard.device)
         dtype = {torch.float32: S.F32, torch.bfloat16: S.BF16}[logits_shard.dtype]
         if history is not None:
             hp, H, hld = history.data_ptr(), history.shape[1], history.stride(0)
         else:
             hp, H, hld = None, 0, 0
-        s = torch.cuda.current_stream(dev)
+        s = torch.cuda.current_stream(logits_shard.device)
         S._check(S.lib().noel_sampler_shard_select(C.byref(cfg), logits_shard.data_ptr(), dtype, B, Vs,
-                                                   logits_shard.stride(0), v_begin, hp, H, hld,
-                                                   entries.data_ptr(), maxes.data_ptr(), flags.data_ptr(),
+                                                   logits_shard.stride(0), v_begin, hp, H, hld, lists.data_ptr(),
                                                    C.c_void_p(s.cuda_stream)))
-        return entries, maxes, flags
+        return lists
 
-    def merge(self, cfg, entries, maxes, flags, rng, probs: bool = False):
+    def merge(self, cfg, lists, rng, probs: bool = False):
+        """lists [n_shards, b, L + 1, 2]; rng [b, 2] int64 advanced in place."""
         import torch
 
-        n, B = maxes.shape
-        dev = maxes.device
-        ids = torch.empty(B, dtype=torch.int32, device=dev)
-        status = torch.empty(B, dtype=torch.int32, device=dev)
-        pr = torch.empty(B, dtype=torch.float32, device=dev) if probs else None
+        n, b = lists.shape[0], lists.shape[1]
+        dev = lists.device
+        assert rng.is_contiguous() and rng.shape[0] == b
+        ids = torch.empty(b, dtype=torch.int32, device=dev)
+        status = torch.empty(b, dtype=torch.int32, device=dev)
+        pr = torch.empty(b, dtype=torch.float32, device=dev) if probs else None
         s = torch.cuda.current_stream(dev)
-        S._check(S.lib().noel_sampler_shard_merge(C.byref(cfg), n, B, entries.data_ptr(), maxes.data_ptr(),
-                                                  flags.data_ptr(), rng.data_ptr(), ids.data_ptr(),
-                                                  pr.data_ptr() if pr is not None else None, status.data_ptr(),
-                                                  C.c_void_p(s.cuda_stream)))
+        S._check(S.lib().noel_sampler_shard_merge(C.byref(cfg), n, b, lists.contiguous().data_ptr(), rng.data_ptr(),
+                                                  ids.data_ptr(), pr.data_ptr() if pr is not None else None,
+                                                  status.data_ptr(), C.c_void_p(s.cuda_stream)))
         return ids, status, pr
 
     def full(self, cfg, rows, rng, history=None, probs: bool = False):
@@ -75,7 +76,7 @@ class CudaKernels:
 
 
 class NcclGather:
-    """Rank-ordered all-gathers over a torch.distributed group (NCCL on GPUs)."""
+    """Rank-ordered collectives over a torch.distributed group (NCCL on GPUs)."""
 
     def __init__(self, group=None):
         import torch.distributed as dist
@@ -96,6 +97,16 @@ class NcclGather:
         parts = [torch.empty_like(t) for _ in range(self.world)]
         self.dist.all_gather(parts, t, group=self.group)
         return torch.stack(parts)
+
+    def all_to_all(self, t, send_rows, recv_rows):
+        """Rows of t split by send_rows go to ranks 0, 1, ...; returns the rows
+        received, in rank order (recv_rows from each)."""
+        import torch
+
+        t = t.contiguous()
+        out = torch.empty((sum(recv_rows),) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        self.dist.all_to_all_single(out, t, list(recv_rows), list(send_rows), group=self.group)
+        return out
 
     def full_rows(self, logits_shard, rows, v_begin: int, vocab: int):
         """The full rows ``rows`` (same index tensor on every rank)."""
@@ -125,10 +136,10 @@ def shard_bounds(vocab: int, world: int):
     return out
 
 
-def _finish(cfg, entries, maxes, flags, rng, history, full_rows, kernels, probs):
-    ids, status, pr = kernels.merge(cfg, entries, maxes, flags, rng, probs)
+def _fallback(cfg, ids, pr, status, rng, history, full_rows, kernels, probs):
+    """Rows with status 1, sampled from their full rows (identical on every rank)."""
     rows = status.nonzero().flatten()
-    if rows.numel():  # identical on every rank: the merge is deterministic
+    if rows.numel():
         rng_sub = rng.index_select(0, rows).contiguous()
         hist_sub = history.index_select(0, rows).contiguous() if history is not None else None
         fid, fpr = kernels.full(cfg, full_rows(rows), rng_sub, hist_sub, probs)
@@ -136,7 +147,7 @@ def _finish(cfg, entries, maxes, flags, rng, history, full_rows, kernels, probs)
         rng[rows] = rng_sub
         if probs:
             pr[rows] = fpr
-    return ids, pr, int(rows.numel())
+    return int(rows.numel())
 
 
 def sample_vocab_sharded(cfg, logits_shard, v_begin: int, vocab: int, rng, history=None, gather=None,
@@ -147,24 +158,44 @@ def sample_vocab_sharded(cfg, logits_shard, v_begin: int, vocab: int, rng, histo
     int64 replicated on every rank and advanced in place; history [B, H]
     int32 global ids (replicated) or None.  Returns (ids [B] int32, probs or
     None, number of rows sampled from their full rows)."""
+    import torch
+
     kernels = kernels or CudaKernels()
     gather = gather or NcclGather()
-    e, m, f = kernels.select(cfg, logits_shard, v_begin, history)
-    E, M, F = gather.all_gather(e), gather.all_gather(m), gather.all_gather(f)
-    return _finish(cfg, E, M, F, rng, history, lambda rows: gather.full_rows(logits_shard, rows, v_begin, vocab),
-                   kernels, probs)
+    world, rank = gather.world, gather.rank
+    B = logits_shard.shape[0]
+    lists = kernels.select(cfg, logits_shard, v_begin, history)  # [B, L + 1, 2]
+    nb = -(-B // world)  # rows merged per rank (the last block may be short)
+    blocks = [(min(r * nb, B), min((r + 1) * nb, B)) for r in range(world)]
+    r0, r1 = blocks[rank]
+    mine = gather.all_to_all(lists, [e - b for b, e in blocks], [r1 - r0] * world)
+    rng_mine = rng[r0:r1].contiguous()
+    ids_m, status_m, pr_m = kernels.merge(cfg, mine.view(world, r1 - r0, *lists.shape[1:]), rng_mine, probs)
+    # one packed row per sampled row: id, status, RNG state (4 x int32), probability bits
+    cols = [ids_m.view(-1, 1), status_m.view(-1, 1), rng_mine.view(torch.int32).view(-1, 4)]
+    if probs:
+        cols.append(pr_m.view(torch.int32).view(-1, 1))
+    packed = torch.zeros(nb, 7 if probs else 6, dtype=torch.int32, device=lists.device)
+    packed[: r1 - r0] = torch.cat(cols, dim=1)
+    allp = gather.all_gather(packed).view(world * nb, -1)[:B]
+    ids = allp[:, 0].contiguous()
+    status = allp[:, 1]
+    rng.copy_(allp[:, 2:6].contiguous().view(torch.int64).view(B, 2))
+    pr = allp[:, 6].contiguous().view(torch.float32) if probs else None
+    n_full = _fallback(cfg, ids, pr, status, rng, history,
+                       lambda rows: gather.full_rows(logits_shard, rows, v_begin, vocab), kernels, probs)
+    return ids, pr, n_full
 
 
 def sample_vocab_sharded_local(cfg, logits, bounds, rng, history=None, probs: bool = False, kernels=None):
     """All shards on one GPU (columns of ``logits`` split by ``bounds``): the
-    same select / merge / fallback steps with the all-gather replaced by a
-    stack, for parity tests and single-GPU use."""
+    same select / merge / fallback steps with the exchange replaced by a
+    stack and every row merged at once, for parity tests and single-GPU use."""
     import torch
 
     kernels = kernels or CudaKernels()
-    parts = [kernels.select(cfg, logits[:, b : b + w], b, history) for b, w in bounds]
-    E = torch.stack([p[0] for p in parts])
-    M = torch.stack([p[1] for p in parts])
-    F = torch.stack([p[2] for p in parts])
-    return _finish(cfg, E, M, F, rng, history, lambda rows: logits.index_select(0, rows).contiguous(), kernels,
-                   probs)
+    lists = torch.stack([kernels.select(cfg, logits[:, b : b + w], b, history) for b, w in bounds])
+    ids, status, pr = kernels.merge(cfg, lists, rng, probs)
+    n_full = _fallback(cfg, ids, pr, status, rng, history, lambda rows: logits.index_select(0, rows).contiguous(),
+                       kernels, probs)
+    return ids, pr, n_full

@@ -14,10 +14,6 @@ pytestmark = pytest.mark.gpu
 PROB_RTOL = 1e-5
 
 
-def _supported(cfgkw):
-    return cfgkw["temperature"] <= 1e-4 or 0 < cfgkw["top_k"] <= 120
-
-
 def run_sharded(device, cfgkw, logits, hist, rng, n_shards):
     import torch
 
@@ -47,14 +43,14 @@ def check(name, cfgkw, logits, hist, rng, oracle, cuda, n_shards):
 
 
 @pytest.mark.parametrize("n_shards", [2, 3, 8])
-@pytest.mark.parametrize("case", [c for c in workload_cases(batch=24) if _supported(c[1])], ids=lambda c: c[0])
+@pytest.mark.parametrize("case", workload_cases(batch=24), ids=lambda c: c[0])
 def test_sharded_workloads_gpu(cuda, oracle, case, n_shards):
     name, cfgkw, logits, hist, rng = case
     check(name, cfgkw, logits, hist, rng, oracle, cuda, n_shards)
 
 
 @pytest.mark.parametrize("n_shards", [2, 5])
-@pytest.mark.parametrize("case", [c for c in edge_cases() if _supported(c[1]) and c[2].shape[1] >= 10],
+@pytest.mark.parametrize("case", [c for c in edge_cases() if c[2].shape[1] >= 10],
                          ids=lambda c: c[0])
 def test_sharded_edge_cases_gpu(cuda, oracle, case, n_shards):
     name, cfgkw, logits, hist, rng = case
@@ -91,13 +87,31 @@ def test_sharded_penalty_lands_in_its_shard_gpu(cuda, oracle):
         check(f"penalty T={T}", _cfg(T=T, k=8, rep=1.3), logits, hist, rng, oracle, cuda, 3)
 
 
-def test_sharded_unsupported_config_gpu(cuda):
-    import torch
+@pytest.mark.parametrize("top_k", [0, 500, 1000])
+def test_sharded_full_list_gpu(cuda, oracle, top_k):
+    """Top-k off or above 120: every shard lists its candidates under its own
+    maximum.  Heavy-tailed rows (few candidates) are decided by the merge;
+    Gaussian rows (candidates everywhere) fall back to their full rows."""
+    from noel_b200.workloads import WORKLOADS, generate_numpy
 
+    w = WORKLOADS["nucleus_bf16"].resized(batch=24, vocab=64000)
+    d = generate_numpy(w, seed=41)
+    cfgkw = dict(w.config_kwargs(), top_k=top_k)
+    n_full = check("heavy tail", cfgkw, d["logits"], None, d["rng"], oracle, cuda, 8)
+    assert n_full < 24  # most rows decided from the lists
+    w2 = WORKLOADS["vocab_sharded"].resized(batch=6, vocab=16000, history=64)
+    d2 = generate_numpy(w2, seed=42)
+    cfg2 = dict(w2.config_kwargs(), top_k=top_k)
+    check("gaussian", cfg2, d2["logits"], d2["history"], d2["rng"], oracle, cuda, 4)
+
+
+def test_sharded_list_len_gpu(cuda):
     from noel_b200 import sampler as S
-    from noel_b200.sharded import sample_vocab_sharded_local
+    from noel_b200.sharded import CudaKernels
 
-    lg = torch.zeros(2, 100, device=cuda)
-    rng = torch.ones(2, 2, dtype=torch.int64, device=cuda)
-    with pytest.raises(S.NoelSamplerError):
-        sample_vocab_sharded_local(S.make_config(top_k=0), lg, [(0, 50), (50, 50)], rng)
+    k = CudaKernels()
+    assert k.list_len(S.make_config(temperature=0.0)) == 1
+    assert k.list_len(S.make_config(top_k=64)) == 72
+    assert k.list_len(S.make_config(top_k=120)) == 128
+    assert k.list_len(S.make_config(top_k=0)) == 256
+    assert k.list_len(S.make_config(top_k=121)) == 256

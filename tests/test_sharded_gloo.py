@@ -1,12 +1,14 @@
 """The collective plumbing of vocab-sharded sampling on two gloo ranks (CPU).
 
 The GPU kernels are replaced by small CPU stand-ins defined here (select: a
-shard's top-K by (value desc, id asc) after a toy penalty; merge: the largest
-gathered value, with every third row left undecided; full row: the argmax of
-the full row).  What is checked is the host logic of noel_b200/sharded.py:
-rank-ordered all-gathers, unequal shard widths, the reconstruction of the
-undecided rows from every rank's columns, RNG states advanced once per row
-whichever path decided it, and identical results on every rank.
+shard's top-K by (value desc, id asc) after a toy penalty, with the trailer of
+its maximum; merge: the largest gathered value, leaving undecided every row
+whose winner has an id divisible by 3; full row: the argmax of the full row).
+What is checked is the host logic of noel_b200/sharded.py: the all-to-all of
+row blocks (including a short last block), the rank-ordered all-gather of the
+results, unequal shard widths, the reconstruction of the undecided rows from
+every rank's columns, RNG states advanced once per row whichever path decided
+it, and identical results on every rank.
 """
 import os
 import socket
@@ -15,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-B, V, K, H = 12, 1001, 4, 6
+B, V, K, H = 13, 1001, 4, 6
 
 
 def _logits_history():
@@ -43,26 +45,28 @@ class FakeKernels:
     def select(self, cfg, logits_shard, v_begin, history):
         x = _penalised(logits_shard.numpy(), v_begin, history.numpy())
         Bn, W = x.shape
-        ent = np.full((Bn, K, 2), -1, np.int32)
+        lists = np.full((Bn, K + 1, 2), -1, np.int32)
         for b in range(Bn):
             order = np.lexsort((np.arange(W), -x[b]))[:K]
-            ent[b, : len(order), 0] = order + v_begin
-            ent[b, : len(order), 1] = x[b, order].view(np.int32)
-        return torch.from_numpy(ent), torch.from_numpy(x.max(axis=1)), torch.zeros(Bn, dtype=torch.int32)
+            lists[b, : len(order), 0] = order + v_begin
+            lists[b, : len(order), 1] = x[b, order].view(np.int32)
+            lists[b, K, 0] = np.float32(x[b].max()).view(np.int32)
+            lists[b, K, 1] = 0
+        return torch.from_numpy(lists)
 
-    def merge(self, cfg, E, M, F, rng, probs):
-        n, Bn = M.shape
+    def merge(self, cfg, lists, rng, probs):
+        n, Bn = lists.shape[0], lists.shape[1]
         ids = torch.zeros(Bn, dtype=torch.int32)
         status = torch.zeros(Bn, dtype=torch.int32)
-        e = E.numpy()
+        e = lists.numpy()
         for b in range(Bn):
-            if b % 3 == 0:
-                status[b] = 1
-                continue
             cand = [(e[s, b, j, 1].view(np.float32), -e[s, b, j, 0]) for s in range(n) for j in range(K)
                     if e[s, b, j, 0] >= 0]
-            best = max(cand)
-            ids[b] = -best[1]
+            best = -max(cand)[1]
+            if best % 3 == 0:
+                status[b] = 1
+                continue
+            ids[b] = best
             rng[b] += 1
         return ids, status, None
 
@@ -121,4 +125,4 @@ def test_sharded_plumbing_two_gloo_ranks(tmp_path):
     for r in (r0, r1):
         np.testing.assert_array_equal(r["ids"], want)
         assert (r["rng"][:, 0] == 1).all()  # one step per row, merged or full-row
-        assert int(r["n_full"]) == len(range(0, B, 3))
+        assert int(r["n_full"]) == int((want % 3 == 0).sum()) > 0
