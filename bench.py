@@ -531,6 +531,61 @@ def run_vocab_sharded(args):
         dist.destroy_process_group()
 
 
+def run_engine_call(args):
+    """The engine's call shape (src/engine.c:378-387): one row of host logits
+    per generated token through noel_sampler_sample, history NULL, with the
+    vocabulary truncated to 8192 (the engine's default) and in full
+    (NOEL_FULL_VOCAB).  Both arms make the same calls on the same row from the
+    same seed, so their id sequences must agree; the reference is its own
+    sampler.c (oracle/_ref) on one host thread, as the engine runs it."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import ctypes as C
+
+    import torch
+
+    from noel_b200 import sampler as S
+    from noel_b200.workloads import WORKLOADS, generate_numpy
+    from oracle.oracle import RefSampler
+
+    torch.cuda.set_device(0)
+    w = WORKLOADS["single_row"]
+    for V in (8192, w.vocab):
+        row = np.ascontiguousarray(generate_numpy(w.resized(vocab=V), seed=3)["logits"][0])  # pageable, like engine.c:59
+        cfg = S.make_config(**dict(w.config_kwargs(), seed=1234))
+        n = max(args.steps, 20) * 4
+        smp = S.Sampler(cfg, max_vocab=V)
+        for _ in range(max(args.warmup, 3) * 4):
+            smp.sample(row)
+        smp.set_config(cfg)  # reseeds (seed != 0, sampler.c:63-70)
+        t0 = time.perf_counter()
+        ids = [smp.sample(row) for _ in range(n)]
+        us = (time.perf_counter() - t0) / n * 1e6
+        line = {"metric": f"us per noel_sampler_sample call, engine call shape (host logits, history NULL), vocab {V}",
+                "value": us, "unit": "us/call", "higher_is_better": False, "calls": n, "dtype": "f32",
+                "data": "synthetic", "config": {"workload": "engine_call", "vocab": V, "temperature": w.temperature,
+                                                "top_k": w.top_k, "top_p": w.top_p, "history": None}}
+        if RefSampler.available():
+            ref = RefSampler()
+            L = ref.lib
+            L.noel_sampler_init.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+            L.noel_sampler_sample.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int]
+            L.noel_sampler_free.argtypes = [C.c_void_p]
+            st = S.SamplerStruct()
+            L.noel_sampler_init(C.byref(st), C.byref(cfg), V)
+            nr = n if V <= 8192 else max(10, n // 8)
+            rrow = row.copy()
+            t0 = time.perf_counter()
+            rids = [L.noel_sampler_sample(C.byref(st), rrow.ctypes.data, V, None, 0) for _ in range(nr)]
+            rus = (time.perf_counter() - t0) / nr * 1e6
+            L.noel_sampler_free(C.byref(st))
+            line["reference"] = {"value": rus, "unit": "us/call", "calls": nr, "cores": 1,
+                                 "kind": "reference", "sample": "src/sampler.c built into oracle/_ref, one thread"}
+            line["parity"] = {"calls": nr, "mismatches": int(sum(a != b for a, b in zip(ids[:nr], rids)))}
+        smp.free()
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -548,6 +603,8 @@ def main():
         run_reference(args)
     elif args.workload == "vocab_sharded":
         run_vocab_sharded(args)
+    elif args.workload == "engine_call":
+        run_engine_call(args)
     else:
         run_ours(args)
 

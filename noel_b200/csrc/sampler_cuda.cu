@@ -60,6 +60,7 @@ struct Workspace {
     int32_t *counters = nullptr;  // 4 ints
     int32_t *rows = nullptr;      // row list of the exact kernel
     uint2 *slots = nullptr;       // nslots x 2 x vocab
+    uint4 *gsplit = nullptr;      // per row: greedy rows split over CTAs (zeroed, re-armed by the kernel)
     int rows_cap = 0, vocab_cap = 0, nslots = 0;
 };
 
@@ -133,12 +134,15 @@ int workspace(DeviceCtx *c, cudaStream_t s, int rows, int vocab, Workspace **out
         cudaFree(w.counters);
         cudaFree(w.rows);
         cudaFree(w.slots);
+        cudaFree(w.gsplit);
         w = Workspace{};
     }
     CUDA_TRY(cudaMalloc(&w.counters, 4 * sizeof(int32_t)));
     CUDA_TRY(cudaMemset(w.counters, 0, 4 * sizeof(int32_t)));
     CUDA_TRY(cudaMalloc(&w.rows, (size_t)rc * sizeof(int32_t)));
     CUDA_TRY(cudaMalloc(&w.slots, (size_t)ns * 2 * (size_t)vc * sizeof(uint2)));
+    CUDA_TRY(cudaMalloc(&w.gsplit, (size_t)rc * sizeof(uint4)));
+    CUDA_TRY(cudaMemset(w.gsplit, 0, (size_t)rc * sizeof(uint4)));
     w.rows_cap = rc;
     w.vocab_cap = vc;
     w.nslots = ns;
@@ -204,7 +208,9 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, bool 
     r = set_smem(c, kexact, smem_exact);
     if (r) return r;
     if (t_ev_before) CUDA_TRY(cudaEventRecord(t_ev_before, s));
-    const int grid = a0.batch;  // one CTA per row (the streaming kernel: one per SM, rows in turn)
+    /* one CTA per row, or per range of a split greedy row (the streaming
+     * kernel: one per SM, rows in turn) */
+    const int grid = a0.gsplit ? a0.batch * a0.split : a0.batch;
     const int sgrid = a0.batch < c->sms ? a0.batch : c->sms;
     if (exact_only) list_all_rows_kernel<<<(a0.batch + 255) / 256 < c->sms ? (a0.batch + 255) / 256 : c->sms, 256, 0,
                                             s>>>(a0);
@@ -440,19 +446,33 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
     if (smem_main > c->smem_optin - 2048 || smem_exact > c->smem_optin - 16384)
         return fail(NOEL_ERR_TOO_LARGE, "vocab %d / history %d need %zu B of shared memory", V, H, smem_main);
 
-    if (fixed_ws) {  // caller-provided scratch (the allocation-free entry point)
-        a.counters = fixed_ws->counters;
-        a.exact_list = fixed_ws->rows;
-        a.slots = fixed_ws->slots;
-        a.nslots = fixed_ws->nslots;
-    } else {
+    const Workspace *ws = fixed_ws;  // caller-provided scratch (the allocation-free entry point)
+    if (!ws) {
         Workspace *w = nullptr;
         r = workspace(c, s, B, V, &w);
         if (r) return r;
-        a.counters = w->counters;
-        a.exact_list = w->rows;
-        a.slots = w->slots;
-        a.nslots = w->nslots;
+        ws = w;
+    }
+    a.counters = ws->counters;
+    a.exact_list = ws->rows;
+    a.slots = ws->slots;
+    a.nslots = ws->nslots;
+    /* greedy rows too few to fill the GPU at 8 CTAs per SM: each row split
+     * into ranges of at least 8192 tokens, one CTA per range, that fold
+     * their best into the row's (the row's last CTA writes it) */
+    if (mode == kGreedy && !so && !stream && ws->gsplit) {
+        const int slots = 8 * c->sms;
+        int sp = B < slots / 2 ? slots / B : 1;
+        sp = sp < 16 ? sp : 16;
+        const int maxsp = V / 8192;
+        sp = sp < maxsp ? sp : maxsp;
+        if (sp > 1) {
+            const int width = (((V + sp - 1) / sp) + 63) & ~63;  // ranges start 256-byte apart from the row's start
+            a.split = (V + width - 1) / width;
+            a.split_vocab = V;
+            a.vocab = width;
+            a.gsplit = ws->gsplit;
+        }
     }
     r = dtype == NOEL_DTYPE_F32
             ? launch_t<float>(a, mode, block_kernel, wide, stream, exact_only, smem_main, smem_exact, c, s)

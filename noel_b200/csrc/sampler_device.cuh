@@ -90,6 +90,10 @@ struct SampleArgs {
      * [s * vocab, s * vocab + vocab) of caller row r / split, s = r % split,
      * of a row of split_vocab columns; 0 or 1: rows are the caller's rows */
     int split, split_vocab;
+    /* greedy rows split over `split` CTAs (no shard output): per caller row,
+     * the best composite key (value desc, id asc) so far, the CTAs done and
+     * NaN at id 0; zero between calls (the row's last CTA re-arms it) */
+    uint4 *gsplit;
     int qcap;                   // queued vectors per warp (single-pass kernel, queued modes)
     /* persistent streaming kernel */
     int nstages;                // shared-memory ring stages of 16 KB

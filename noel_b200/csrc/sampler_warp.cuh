@@ -135,7 +135,7 @@ __device__ __forceinline__ void hs_penalize(const HistSet &h, uint32_t id0, floa
 /* penalised values written back to the caller's fp32 row, once per distinct id */
 template <int NT>
 __device__ void hs_write_back(const SampleArgs &a, const HistSet &h, int row) {
-    float *wrow = a.wb + (size_t)row * a.ld;
+    float *wrow = a.wb + (size_t)row_span(a, row).off;
     for (int s = threadIdx.x; s < h.cap; s += NT) {
         const uint32_t k = h.key[s];
         if (k) wrow[k - 1] = __uint_as_float(h.val[s]);
@@ -646,8 +646,28 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
                     bx = rs.gx[w];
                     bid = rs.gid[w];
                 }
+            int orow = row;
+            bool nan0 = rs.l0nan;
+            if (a.gsplit) {
+                /* a range of a split row: fold this range's best into the
+                 * row's; the row's last CTA writes the result and re-arms */
+                const RowSpan sp = row_span(a, row);
+                uint4 *gs = a.gsplit + sp.hrow;
+                unsigned long long *best = reinterpret_cast<unsigned long long *>(gs);
+                if (bid != 0xFFFFFFFFu) atomicMax(best, comp_key(ord_key(bx), bid + (uint32_t)sp.id_off));
+                if (sp.id_off == 0 && rs.l0nan) atomicExch(&gs->w, 1u);
+                __threadfence();
+                if (atomicAdd(&gs->z, 1u) != (uint32_t)a.split - 1u) return;
+                __threadfence();
+                const unsigned long long b = atomicExch(best, 0ull);
+                nan0 = atomicExch(&gs->w, 0u) != 0u;
+                gs->z = 0u;
+                bid = b ? 0xFFFFFFFFu - (uint32_t)b : 0xFFFFFFFFu;
+                orow = sp.hrow;
+            }
+            const int row = orow;
             RowOut o;
-            o.id = (rs.l0nan || bid == 0xFFFFFFFFu) ? 0 : (int)bid;  // sampler.c:106-116
+            o.id = (nan0 || bid == 0xFFFFFFFFu) ? 0 : (int)bid;  // sampler.c:106-116
             o.prob = 1.0f;
             o.mass = 1.0f;
             o.n_topk = o.n_final = o.num_cands = 1;
