@@ -586,6 +586,112 @@ def run_engine_call(args):
         print(json.dumps(line), flush=True)
 
 
+def run_router(args):
+    """The MoE router (src/sparsity.c:46-79) over a batch of tokens: 1,048,576
+    tokens x 64 experts fp32 gate logits N(0, 3^2) (268 MB, larger than L2),
+    top-8, per GPU.  value = routed tokens/s; the roofline is HBM (the logits
+    read once, 8 B per routing entry written).  The reference's
+    aether_route_top_k is timed on a bounded sample on the host cores and its
+    ids are compared with the GPU's."""
+    import torch
+
+    from noel_b200 import sampler as S
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    T, E, K = (args.batch or 1048576), 64, 8
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn(T, E, device=dev, generator=g) * 3.0
+    stream = torch.cuda.current_stream(dev)
+    out = torch.empty(T, K, 2, dtype=torch.int32, device=dev)
+
+    def step():
+        S._check(S.lib().noel_moe_route_top_k(x.data_ptr(), T, E, E, K, out.data_ptr(),
+                                              S.C.c_void_p(stream.cuda_stream)))
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if args.profile:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        return
+    clocks = ClockSampler(local if world > 1 else torch.cuda.current_device())
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    t_ms = reduce_max(e0.elapsed_time(e1), world)
+    value = T * world * args.steps / (t_ms / 1e3)
+    k_ms = t_ms / args.steps
+    peak, peak_kind = measured_peak()
+    bytes_per_launch = T * E * 4 + T * K * 8
+    achieved = bytes_per_launch / (k_ms / 1e3) / 1e9
+    # end to end through the public Python API from pinned host memory
+    h_x = x.cpu().pin_memory()
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        ids, w = S.route_top_k(h_x.to(dev, non_blocking=True), K)
+        ids.cpu(), w.cpu()
+    e2e_s = reduce_max(time.perf_counter() - t0, world)
+    cpu, parity = None, None
+    if rank == 0 and not args.no_cpu:
+        from oracle.oracle import RefAux
+
+        if RefAux.available():
+            n = min(T, 65536)
+            xs = h_x[:n].numpy()
+            ref = RefAux()
+            ref.route_batch(xs[:1024], K)  # warm
+            t0 = time.perf_counter()
+            rid, _ = ref.route_batch(xs, K)
+            rps = n / (time.perf_counter() - t0)
+            step()
+            torch.cuda.synchronize()
+            gid = out[:n, :, 0].cpu().numpy()
+            parity = {"tokens": n, "mismatches": int((gid != rid).any(axis=1).sum()),
+                      "against": "the reference's src/sparsity.c built into oracle/_ref"}
+            if parity["mismatches"]:
+                print(json.dumps({"error": "parity", "parity": parity}), flush=True)
+                sys.exit(1)
+            cpu = {"value": rps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"{n} tokens through aether_route_top_k, OpenMP over tokens"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"routed tokens/s, MoE router {E} experts top-{K} fp32", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": t_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "moe_router", "tokens_per_gpu": T, "experts": E, "top_k": K,
+                       "parallelism": f"token-sharded x{world}",
+                       "l2": f"no flush: {T * E * 4 / 1e6:.0f} MB of gate logits per step > 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "kernel": "moe_route_kernel", "kernel_ms": k_ms,
+                         "bytes_per_launch": bytes_per_launch, "peak_source": f"{peak_kind} hbm_gbs"},
+            "cpu_baseline": cpu, "parity": parity,
+            "e2e": {"value": T * world * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * E * 4,
+                    "d2h_bytes_per_step": T * K * 8, "steps": e2e_steps,
+                    "api": "noel_b200.sampler.route_top_k from pinned host logits"},
+            "clocks": clk, "gpu_launches": args.steps,
+        }), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -605,6 +711,8 @@ def main():
         run_vocab_sharded(args)
     elif args.workload == "engine_call":
         run_engine_call(args)
+    elif args.workload == "moe_router":
+        run_router(args)
     else:
         run_ours(args)
 

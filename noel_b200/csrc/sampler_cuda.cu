@@ -21,7 +21,9 @@
 #include <mutex>
 #include <vector>
 
+#include "noel_router.h"
 #include "noel_sampler_cuda.h"
+#include "router.cuh"
 #include "sampler_stream.cuh"
 
 #define NOEL_EXPF_QUAL static __device__ const
@@ -790,6 +792,37 @@ thread_local HostBatchStage t_hb;
 }  // namespace
 
 /* ------------------------------------------------------ vocab-sharded rows */
+extern "C" int noel_moe_route_top_k(const float *d_gate_logits, int n_tokens, int n_experts, size_t ld, int top_k,
+                                    noel_moe_routing_t *d_routing, void *stream) {
+    if (n_tokens < 0) return fail(NOEL_ERR_INVALID_ARG, "n_tokens %d", n_tokens);
+    if (n_experts < 1 || n_experts > kRouterMaxExperts)
+        return fail(NOEL_ERR_TOO_LARGE, "n_experts %d (1..%d)", n_experts, kRouterMaxExperts);
+    if (top_k < 1 || top_k > kRouterMaxTopK) return fail(NOEL_ERR_TOO_LARGE, "top_k %d (1..%d)", top_k, kRouterMaxTopK);
+    if (ld < (size_t)n_experts) return fail(NOEL_ERR_INVALID_ARG, "ld %zu < n_experts %d", ld, n_experts);
+    if (n_tokens == 0) return ok();
+    if (!d_gate_logits || !d_routing) return fail(NOEL_ERR_INVALID_ARG, "gate logits and routing are required");
+    if ((reinterpret_cast<uintptr_t>(d_gate_logits) & 3) || (reinterpret_cast<uintptr_t>(d_routing) & 7))
+        return fail(NOEL_ERR_INVALID_ARG, "gate logits must be 4-byte and routing 8-byte aligned");
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    RouterArgs ra{};
+    ra.logits = d_gate_logits;
+    ra.ld = (int64_t)ld;
+    ra.tokens = n_tokens;
+    ra.experts = n_experts;
+    ra.top_k = top_k;
+    ra.out = reinterpret_cast<uint2 *>(d_routing);
+    ra.et = c->et;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int tgrid = (n_tokens + kRouterThreads - 1) / kRouterThreads;
+    if (top_k <= 8) moe_route_thread_kernel<8><<<tgrid, kRouterThreads, 0, s>>>(ra);
+    else if (top_k <= 16) moe_route_thread_kernel<16><<<tgrid, kRouterThreads, 0, s>>>(ra);
+    else moe_route_kernel<<<(n_tokens + kRouterWarps - 1) / kRouterWarps, 32 * kRouterWarps, 0, s>>>(ra);
+    CUDA_TRY(cudaGetLastError());
+    return ok();
+}
+
 extern "C" int noel_sampler_shard_list_len(const noel_sampler_config_t *cfg) {
     if (!cfg) return fail(NOEL_ERR_INVALID_ARG, "cfg is NULL");
     return shard_plan(cfg).len;

@@ -115,6 +115,8 @@ def lib() -> C.CDLL:
         C.POINTER(SamplerConfig), C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
         C.c_void_p, C.c_void_p,
     ]
+    L.noel_moe_route_top_k.restype = C.c_int
+    L.noel_moe_route_top_k.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_int, C.c_void_p, C.c_void_p]
     L.noel_sampler_cuda_last_error.restype = C.c_int
     L.noel_sampler_cuda_last_error_message.restype = C.c_char_p
     L.noel_sampler_cuda_status_string.restype = C.c_char_p
@@ -319,3 +321,18 @@ def expf_checksums(chunk_log2: int = 24):
     _check(lib().noel_sampler_cuda_expf_checksums(chunk_log2, out.data_ptr(), C.c_void_p(s.cuda_stream)))
     s.synchronize()
     return out.cpu().numpy().view(np.uint64)
+
+
+def route_top_k(gate_logits, top_k: int):
+    """MoE routing of every row of gate_logits (a CUDA float32 tensor [T, E],
+    unit column stride): the reference's aether_route_top_k per token.
+    Returns (expert ids [T, top_k] int32, weights [T, top_k] float32)."""
+    import torch
+
+    assert gate_logits.is_cuda and gate_logits.dtype == torch.float32 and gate_logits.stride(1) == 1
+    T, E = gate_logits.shape
+    out = torch.empty(T, top_k, 2, dtype=torch.int32, device=gate_logits.device)
+    s = torch.cuda.current_stream(gate_logits.device)
+    _check(lib().noel_moe_route_top_k(gate_logits.data_ptr(), T, E, gate_logits.stride(0), top_k, out.data_ptr(),
+                                      C.c_void_p(s.cuda_stream)))
+    return out[:, :, 0], out[:, :, 1].view(torch.float32)

@@ -20,6 +20,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libsampler_ref.so")
+REF_AUX_SO = os.path.join(HERE, "_ref", "libaux_ref.so")
 
 
 class SamplerConfig(C.Structure):
@@ -126,6 +127,9 @@ class Oracle:
             C.POINTER(C.c_int32), C.POINTER(C.c_float), C.c_void_p,
             C.POINTER(C.c_int32), C.POINTER(C.c_float), C.c_int, C.c_int,
         ]
+        L.orc_route_top_k.restype = None
+        L.orc_route_top_k.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t, C.c_int,
+                                      C.POINTER(C.c_int32), C.POINTER(C.c_float)]
         L.orc_random_f32.restype = C.c_float
         L.orc_random_f32.argtypes = [C.POINTER(C.c_uint64)]
         L.orc_expf_range.restype = None
@@ -168,6 +172,16 @@ class Oracle:
                                       _ptr(tn_ids, C.c_int32), _ptr(tn_p, C.c_float), n_list,
                                       1 if in_place else 0, nthreads)
         return BatchResult(ids=ids, rng=rng, probs=probs, diag=diag, topn_ids=tn_ids, topn_probs=tn_p)
+
+    def route_top_k(self, logits: np.ndarray, top_k: int):
+        """sparsity.c:46-79 for every row of logits [T, E]: (ids [T, top_k],
+        weights [T, top_k])."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        T, E = x.shape
+        ids = np.empty((T, top_k), np.int32)
+        w = np.empty((T, top_k), np.float32)
+        self.lib.orc_route_top_k(_ptr(x, C.c_float), T, E, E, top_k, _ptr(ids, C.c_int32), _ptr(w, C.c_float))
+        return ids, w
 
     def expf(self, x: np.ndarray) -> np.ndarray:
         """glibc expf on an arbitrary float32 array (via contiguous bit ranges)."""
@@ -247,3 +261,49 @@ class RefSampler:
                                   _ptr(ids, C.c_int32), _ptr(nc, C.c_int32), _ptr(ci, C.c_int32),
                                   _ptr(cv, C.c_float), n_list, 1 if in_place else 0, nthreads)
         return BatchResult(ids=ids, rng=rng, num_cands=nc, topn_ids=ci, cand_vals=cv)
+
+
+class RoutingEntry(C.Structure):
+    """moe_routing_t (reference include/sparsity.h:12-15)."""
+
+    _fields_ = [("expert_id", C.c_int32), ("weight", C.c_float)]
+
+
+class RefAux:
+    """The reference's router and pipeline samplers themselves
+    (oracle/_ref/libaux_ref.so: src/sparsity.c, src/pipeline_stages.c)."""
+
+    def __init__(self, path: str = REF_AUX_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = C.CDLL(path)
+        self.lib.aether_route_top_k.restype = None
+        self.lib.aether_route_top_k.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.POINTER(RoutingEntry)]
+        self.lib.ref_route_batch.restype = None
+        self.lib.ref_route_batch.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t, C.c_int,
+                                             C.c_void_p, C.c_int]
+
+    @staticmethod
+    def available(path: str = REF_AUX_SO) -> bool:
+        return os.path.exists(path)
+
+    def route_top_k(self, logits: np.ndarray, top_k: int):
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        T, E = x.shape
+        ids = np.empty((T, top_k), np.int32)
+        w = np.empty((T, top_k), np.float32)
+        out = (RoutingEntry * top_k)()
+        for t in range(T):
+            self.lib.aether_route_top_k(x[t].ctypes.data_as(C.POINTER(C.c_float)), E, top_k, out)
+            ids[t] = [e.expert_id for e in out]
+            w[t] = [e.weight for e in out]
+        return ids, w
+
+    def route_batch(self, logits: np.ndarray, top_k: int, nthreads: int = 0):
+        """ref_route_batch (aux_driver.c): the reference router over every row
+        with OpenMP; returns (ids, weights)."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        T, E = x.shape
+        out = np.empty((T, top_k, 2), np.int32)
+        self.lib.ref_route_batch(x.ctypes.data_as(C.POINTER(C.c_float)), T, E, E, top_k, out.ctypes.data, nthreads)
+        return out[:, :, 0].copy(), out[:, :, 1].copy().view(np.float32)
