@@ -24,8 +24,9 @@ typedef struct {
  * n_experts, top_k)[k] for t in [0, n_tokens): the top_k experts by (logit
  * desc, id asc) among logits strictly above -1e9 (then (-1, weight of a -1e9
  * slot) slots), with softmax weights over the selected logits.  Expert ids
- * are exact; weights are within one fp32 unit of the reference's (the C
- * library's expf below -15).  1 <= n_experts <= 256, 1 <= top_k <= 64,
+ * are exact; weights are within 1e-5 relative of the reference's (CUDA's
+ * single-precision expf, within 2 units in the last place of the C
+ * library's).  1 <= n_experts <= 256, 1 <= top_k <= 64,
  * ld >= n_experts.  Returns NOEL_OK or a negative status
  * (noel_sampler_cuda_last_error_message() says why).  Asynchronous on stream.
  */

@@ -18,9 +18,8 @@
  *
  * Weights (sparsity.c:67-78): expf(w - max) with max the first slot's value,
  * summed in slot order in fp32, times 1/sum (0 when the sum is not > 0).
- * expf is the C library's for arguments in (-15, 0] (the sampler's table of
- * its exceptions) and exp rounded to fp32 below, within one unit in the last
- * place of the C library's.
+ * expf is CUDA's single-precision expf, within 2 units in the last place of
+ * the C library's.
  */
 #pragma once
 
@@ -40,10 +39,10 @@ struct RouterArgs {
     ExpTable et;
 };
 
-__device__ __forceinline__ float router_expf(float d, const ExpTable &et) {
-    if (d > -15.0f && d <= 0.0f) return ref_weight(d, et);
-    return (float)exp((double)d);
-}
+/* CUDA's single-precision expf: within 2 units in the last place of the C
+ * library's (weights within 1e-5 relative) at a fraction of the cost of the
+ * sampler's bit-exact double-precision path on B200's fp64 pipe */
+__device__ __forceinline__ float router_expf(float d, const ExpTable &) { return expf(d); }
 
 constexpr int kRouterThreads = 128;
 

@@ -21,8 +21,10 @@
 #include <mutex>
 #include <vector>
 
+#include "noel_postreq.h"
 #include "noel_router.h"
 #include "noel_sampler_cuda.h"
+#include "postreq.cuh"
 #include "router.cuh"
 #include "sampler_stream.cuh"
 
@@ -792,6 +794,164 @@ thread_local HostBatchStage t_hb;
 }  // namespace
 
 /* ------------------------------------------------------ vocab-sharded rows */
+/* ------------------------------------------------ the pipeline's sampler */
+static_assert(sizeof(noel_postreq_params_t) == 24, "aether_sampling_params_t layout");
+
+extern "C" int noel_postreq_sample_batch(const noel_postreq_params_t *params, float *d_logits, int batch, int vocab,
+                                         size_t ld, const float *d_uniform, int32_t *d_ids, void *stream) {
+    if (!params) return fail(NOEL_ERR_INVALID_ARG, "params is NULL");
+    if (batch < 0 || vocab <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", batch, vocab);
+    if (ld < (size_t)vocab) return fail(NOEL_ERR_INVALID_ARG, "ld %zu < vocab %d", ld, vocab);
+    if (batch == 0) return ok();
+    if (!d_logits || !d_ids || (!d_uniform && params->temperature > 1e-4f))
+        return fail(NOEL_ERR_INVALID_ARG, "logits, ids and (non-greedy) uniforms are required");
+    if (reinterpret_cast<uintptr_t>(d_logits) & 3) return fail(NOEL_ERR_INVALID_ARG, "logits not 4-byte aligned");
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    PostArgs pa{};
+    pa.logits = d_logits;
+    pa.ld = (int64_t)ld;
+    pa.batch = batch;
+    pa.vocab = vocab;
+    pa.temperature = params->temperature;
+    pa.top_p = params->top_p;
+    pa.top_k = params->top_k;
+    pa.uniform = d_uniform;
+    pa.ids = d_ids;
+    pa.et = c->et;
+    postreq_sample_kernel<<<batch, kPostThreads, 0, static_cast<cudaStream_t>(stream)>>>(pa);
+    CUDA_TRY(cudaGetLastError());
+    return ok();
+}
+
+extern "C" int noel_postreq_apply_penalties_batch(float *d_logits, int batch, int vocab, size_t ld,
+                                                  const int32_t *d_history, int history_len, size_t hld,
+                                                  float penalty, int window, void *stream) {
+    if (batch < 0 || vocab <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", batch, vocab);
+    if (penalty <= 1.0f || history_len <= 0 || batch == 0) return ok();  // pipeline_stages.c:67
+    if (!d_logits || !d_history) return fail(NOEL_ERR_INVALID_ARG, "logits and history are required");
+    if (ld < (size_t)vocab || hld < (size_t)history_len) return fail(NOEL_ERR_INVALID_ARG, "ld / hld too small");
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    const int start = (window > 0 && history_len > window) ? history_len - window : 0;  // pipeline_stages.c:69
+    const int n = history_len - start;
+    const int cap = pow2_at_least(2 * n > 64 ? 2 * n : 64);
+    const size_t smem = (size_t)cap * 8;
+    if (smem > c->smem_optin - 1024) return fail(NOEL_ERR_TOO_LARGE, "history window %d", n);
+    r = set_smem(c, (const void *)postreq_penalty_kernel, smem);
+    if (r) return r;
+    postreq_penalty_kernel<<<batch, kPostThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+        d_logits, (int64_t)ld, vocab, d_history, (int64_t)hld, history_len, start, penalty, cap);
+    CUDA_TRY(cudaGetLastError());
+    return ok();
+}
+
+extern "C" int noel_postreq_grammar_mask_batch(float *d_logits, int batch, int vocab, size_t ld,
+                                               const int32_t *d_fsm_state, int fsm_state, void *stream) {
+    if (batch < 0 || vocab <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch %d / vocab %d", batch, vocab);
+    if (batch == 0) return ok();
+    if (!d_logits || ld < (size_t)vocab) return fail(NOEL_ERR_INVALID_ARG, "logits / ld");
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    const size_t n = (size_t)batch * (size_t)vocab;
+    const size_t want = (n + 255) / 256;
+    const int grid = (int)(want < (size_t)(c->sms * 8) ? want : (size_t)(c->sms * 8));
+    postreq_grammar_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_logits, (int64_t)ld, batch, vocab,
+                                                                               d_fsm_state, fsm_state);
+    CUDA_TRY(cudaGetLastError());
+    return ok();
+}
+
+namespace {
+/* per-thread buffers of the single-row pipeline sampler */
+struct PostStage {
+    int dev = -1;
+    float *d_row = nullptr, *h_row = nullptr, *d_u = nullptr;
+    int32_t *d_id = nullptr, *h_id = nullptr;
+    int cap = 0;
+    cudaStream_t stream = nullptr;
+    void release() {
+        if (dev < 0) return;
+        int cur = 0;
+        cudaGetDevice(&cur);
+        cudaSetDevice(dev);
+        if (stream) cudaStreamSynchronize(stream);
+        cudaFree(d_row);
+        cudaFree(d_u);
+        cudaFree(d_id);
+        cudaFreeHost(h_row);
+        cudaFreeHost(h_id);
+        if (stream) cudaStreamDestroy(stream);
+        cudaSetDevice(cur);
+        *this = PostStage{};
+    }
+    ~PostStage() { release(); }
+};
+thread_local PostStage t_post;
+}  // namespace
+
+extern "C" int32_t noel_postreq_sample(float *logits, int vocab_size, const noel_postreq_params_t *params) {
+    if (!logits || vocab_size <= 0 || !params) {
+        fail(NOEL_ERR_INVALID_ARG, "logits, vocab_size and params are required");
+        return 0;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        fail(NOEL_ERR_NO_DEVICE, "no CUDA device");
+        return 0;
+    }
+    PostStage &st = t_post;
+    if (st.dev != dev) st.release();
+    const bool greedy = params->temperature <= 1e-4f;
+    /* the reference draws once, after the softmax, on non-greedy calls
+     * (pipeline_stages.c:180); drawing here keeps the caller's rand() stream
+     * where the reference would leave it */
+    const float u = greedy ? 0.0f : (float)rand() / (float)RAND_MAX;
+    auto step = [&]() -> int {
+        if (!st.stream) {
+            st.dev = dev;
+            CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
+            CUDA_TRY(cudaMalloc(&st.d_u, sizeof(float)));
+            CUDA_TRY(cudaMalloc(&st.d_id, sizeof(int32_t)));
+            CUDA_TRY(cudaMallocHost(&st.h_id, sizeof(int32_t)));
+        }
+        const bool on_dev = is_device_ptr(logits);
+        float *row = logits;
+        if (!on_dev) {
+            if (st.cap < vocab_size) {
+                cudaFree(st.d_row);
+                cudaFreeHost(st.h_row);
+                st.d_row = nullptr;
+                st.h_row = nullptr;
+                st.cap = 0;
+                CUDA_TRY(cudaMalloc(&st.d_row, (size_t)vocab_size * sizeof(float)));
+                CUDA_TRY(cudaMallocHost(&st.h_row, (size_t)vocab_size * sizeof(float)));
+                st.cap = vocab_size;
+            }
+            memcpy(st.h_row, logits, (size_t)vocab_size * sizeof(float));
+            CUDA_TRY(cudaMemcpyAsync(st.d_row, st.h_row, (size_t)vocab_size * sizeof(float), cudaMemcpyHostToDevice,
+                                     st.stream));
+            row = st.d_row;
+        }
+        CUDA_TRY(cudaMemcpyAsync(st.d_u, &u, sizeof(float), cudaMemcpyHostToDevice, st.stream));
+        int r2 = noel_postreq_sample_batch(params, row, 1, vocab_size, (size_t)vocab_size, st.d_u, st.d_id, st.stream);
+        if (r2) return r2;
+        CUDA_TRY(cudaMemcpyAsync(st.h_id, st.d_id, sizeof(int32_t), cudaMemcpyDeviceToHost, st.stream));
+        if (!on_dev && !greedy)  // the row now holds the probabilities, as in the reference
+            CUDA_TRY(cudaMemcpyAsync(st.h_row, st.d_row, (size_t)vocab_size * sizeof(float), cudaMemcpyDeviceToHost,
+                                     st.stream));
+        CUDA_TRY(cudaStreamSynchronize(st.stream));
+        if (!on_dev && !greedy) memcpy(logits, st.h_row, (size_t)vocab_size * sizeof(float));
+        return NOEL_OK;
+    };
+    if (step() != NOEL_OK) return 0;
+    ok();
+    return *st.h_id;
+}
+
 extern "C" int noel_moe_route_top_k(const float *d_gate_logits, int n_tokens, int n_experts, size_t ld, int top_k,
                                     noel_moe_routing_t *d_routing, void *stream) {
     if (n_tokens < 0) return fail(NOEL_ERR_INVALID_ARG, "n_tokens %d", n_tokens);

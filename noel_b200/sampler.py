@@ -115,6 +115,17 @@ def lib() -> C.CDLL:
         C.POINTER(SamplerConfig), C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
         C.c_void_p, C.c_void_p,
     ]
+    L.noel_postreq_sample_batch.restype = C.c_int
+    L.noel_postreq_sample_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_void_p,
+                                            C.c_void_p, C.c_void_p]
+    L.noel_postreq_apply_penalties_batch.restype = C.c_int
+    L.noel_postreq_apply_penalties_batch.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int,
+                                                     C.c_size_t, C.c_float, C.c_int, C.c_void_p]
+    L.noel_postreq_grammar_mask_batch.restype = C.c_int
+    L.noel_postreq_grammar_mask_batch.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_void_p, C.c_int,
+                                                  C.c_void_p]
+    L.noel_postreq_sample.restype = C.c_int32
+    L.noel_postreq_sample.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
     L.noel_moe_route_top_k.restype = C.c_int
     L.noel_moe_route_top_k.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_int, C.c_void_p, C.c_void_p]
     L.noel_sampler_cuda_last_error.restype = C.c_int
@@ -336,3 +347,64 @@ def route_top_k(gate_logits, top_k: int):
     _check(lib().noel_moe_route_top_k(gate_logits.data_ptr(), T, E, gate_logits.stride(0), top_k, out.data_ptr(),
                                       C.c_void_p(s.cuda_stream)))
     return out[:, :, 0], out[:, :, 1].view(torch.float32)
+
+
+class PostreqParams(C.Structure):
+    """noel_postreq_params_t (include/noel_postreq.h; the reference's
+    aether_sampling_params_t, include/pipeline_stages.h:13-20)."""
+
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int),
+                ("repetition_penalty", C.c_float), ("repetition_window", C.c_int),
+                ("grammar_enforce_json", C.c_bool)]
+
+
+def postreq_params(temperature=0.7, top_p=0.9, top_k=50, repetition_penalty=1.15, repetition_window=2048,
+                   grammar_enforce_json=False) -> PostreqParams:
+    return PostreqParams(temperature, top_p, top_k, repetition_penalty, repetition_window, grammar_enforce_json)
+
+
+def postreq_sample_batch(logits, params: PostreqParams, uniforms):
+    """aether_postreq_sample on every row of logits (CUDA float32 [B, V],
+    unit column stride; modified in place as the reference modifies its row)
+    with the rows' uniforms (CUDA float32 [B]).  Returns ids [B] int32."""
+    import torch
+
+    assert logits.is_cuda and logits.dtype == torch.float32 and logits.stride(1) == 1
+    B, V = logits.shape
+    ids = torch.empty(B, dtype=torch.int32, device=logits.device)
+    s = torch.cuda.current_stream(logits.device)
+    _check(lib().noel_postreq_sample_batch(C.byref(params), logits.data_ptr(), B, V, logits.stride(0),
+                                           uniforms.data_ptr() if uniforms is not None else None, ids.data_ptr(),
+                                           C.c_void_p(s.cuda_stream)))
+    return ids
+
+
+def postreq_apply_penalties_batch(logits, history, penalty: float, window: int) -> None:
+    import torch
+
+    B, V = logits.shape
+    s = torch.cuda.current_stream(logits.device)
+    _check(lib().noel_postreq_apply_penalties_batch(logits.data_ptr(), B, V, logits.stride(0), history.data_ptr(),
+                                                    history.shape[1], history.stride(0), penalty, window,
+                                                    C.c_void_p(s.cuda_stream)))
+
+
+def postreq_grammar_mask_batch(logits, states=None, state: int = 0) -> None:
+    import torch
+
+    B, V = logits.shape
+    s = torch.cuda.current_stream(logits.device)
+    _check(lib().noel_postreq_grammar_mask_batch(logits.data_ptr(), B, V, logits.stride(0),
+                                                 states.data_ptr() if states is not None else None, state,
+                                                 C.c_void_p(s.cuda_stream)))
+
+
+def postreq_sample(logits, params: PostreqParams) -> int:
+    """The drop-in single-row call (host numpy float32 row or CUDA tensor),
+    drawing rand() where the reference does."""
+    lp, V = _ptr_len(logits)
+    r = lib().noel_postreq_sample(lp, V, C.byref(params))
+    st = lib().noel_sampler_cuda_last_error()
+    if st != 0:
+        _check(st)
+    return int(r)

@@ -1,13 +1,15 @@
 /*
- * Oracle for the paths next to the sampler: a CPU restatement of the
- * reference's MoE router (Sain-Kai/noel src/sparsity.c:46-79), used ONLY as
- * the checker by tests/ and bench.py's CPU leg.  Nothing in the shipped
- * library links, loads or calls this code.
+ * Oracle for the paths next to the sampler: CPU restatements of the
+ * reference's MoE router (Sain-Kai/noel src/sparsity.c:46-79) and of the
+ * pipeline's sibling sampler (src/pipeline_stages.c:64-189), used ONLY as
+ * checkers by tests/ and bench.py's CPU leg.  Nothing in the shipped library
+ * links, loads or calls this code.
  *
- * Parity pinning: checked against the reference's known-answer test
- * (tests/test_engine.c:128-142) and against the reference's own sparsity.c,
- * compiled from its sources into oracle/_ref/libaux_ref.so by
- * oracle/Makefile, on seeded inputs (tests/test_router.py).
+ * Parity pinning: checked against the reference's known-answer test of the
+ * router (tests/test_engine.c:128-142) and against the reference's own
+ * sparsity.c and pipeline_stages.c, compiled from their sources into
+ * oracle/_ref/libaux_ref.so by oracle/Makefile, on seeded inputs
+ * (tests/test_router.py, tests/test_postreq.py).
  */
 #include <math.h>
 #include <stddef.h>
@@ -47,4 +49,94 @@ void orc_route_top_k(const float *logits, int T, int E, size_t ld, int top_k, in
         const float inv = sum > 0.0f ? (1.0f / sum) : 0.0f;
         for (int k = 0; k < top_k; ++k) w[k] *= inv;
     }
+}
+
+/* ------------------------------------------------------------------------ */
+/* the pipeline's sibling sampler (src/pipeline_stages.c:64-189)            */
+
+/* pipeline_stages.c:64-79: per occurrence, in place, ids outside [0, V) skipped */
+void orc_postreq_apply_penalties(float *logits, int V, const int32_t *hist, int H, float pen, int window) {
+    if (pen <= 1.0f || H <= 0) return;
+    const int first = (window > 0 && H > window) ? H - window : 0;
+    for (int i = first; i < H; ++i) {
+        const int32_t t = hist[i];
+        if (t < 0 || t >= V) continue;
+        logits[t] = logits[t] > 0.0f ? logits[t] / pen : logits[t] * pen;
+    }
+}
+
+/* pipeline_stages.c:81-94: state 0 keeps only '{' */
+void orc_postreq_grammar_mask(float *logits, int V, int state) {
+    if (state != 0) return;
+    for (int v = 0; v < V; ++v)
+        if (v != '{') logits[v] = -1e9f;
+}
+
+/* pipeline_stages.c:103-189 with the uniform r given (the reference draws it
+ * from rand() at :180); the row is modified in place as the reference does */
+int32_t orc_postreq_sample(float *logits, int V, float T, float top_p, int top_k, float r) {
+    if (T <= 1e-4f) { /* :105-115 first strict maximum */
+        int32_t best = 0;
+        float bv = logits[0];
+        for (int v = 1; v < V; ++v)
+            if (logits[v] > bv) {
+                bv = logits[v];
+                best = v;
+            }
+        return best;
+    }
+    const float inv_t = 1.0f / T; /* :118-121 */
+    for (int v = 0; v < V; ++v) logits[v] *= inv_t;
+    float m = logits[0]; /* :124-127 */
+    for (int v = 1; v < V; ++v)
+        if (logits[v] > m) m = logits[v];
+    float sum = 0.0f; /* :128-136 */
+    for (int v = 0; v < V; ++v) {
+        logits[v] = expf(logits[v] - m);
+        sum += logits[v];
+    }
+    const float inv_sum = sum > 0.0f ? 1.0f / sum : 0.0f;
+    for (int v = 0; v < V; ++v) logits[v] *= inv_sum;
+    int K = top_k; /* :138-158: the K best by (p desc, id asc), slots of (-1, -1) */
+    if (K <= 0 || K > V) K = V;
+    if (K > 256) K = 256;
+    int32_t cid[256];
+    float cp[256];
+    for (int i = 0; i < K; ++i) {
+        cid[i] = -1;
+        cp[i] = -1.0f;
+    }
+    for (int v = 0; v < V; ++v) {
+        const float p = logits[v];
+        if (!(p > cp[K - 1])) continue;
+        int at = K - 1; /* below every slot it does not strictly beat */
+        while (at > 0 && p > cp[at - 1]) {
+            cp[at] = cp[at - 1];
+            cid[at] = cid[at - 1];
+            --at;
+        }
+        cp[at] = p;
+        cid[at] = v;
+    }
+    float cum = 0.0f; /* :160-168 */
+    int n = 0;
+    for (int i = 0; i < K && cid[i] >= 0; ++i) {
+        cum += cp[i];
+        ++n;
+        if (cum >= top_p) break;
+    }
+    const float inv_cum = 1.0f / cum; /* :170-174 */
+    for (int i = 0; i < n; ++i) cp[i] *= inv_cum;
+    float run = 0.0f; /* :180-188 */
+    for (int i = 0; i < n; ++i) {
+        run += cp[i];
+        if (r <= run || i == n - 1) return cid[i];
+    }
+    return cid[0];
+}
+
+/* B rows (row b at logits + b * ld), uniforms r[b] */
+void orc_postreq_sample_batch(float *logits, int B, int V, size_t ld, float T, float top_p, int top_k, const float *r,
+                              int32_t *ids) {
+    for (int b = 0; b < B; ++b) ids[b] = orc_postreq_sample(logits + (size_t)b * ld, V, T, top_p, top_k, r[b]);
 }

@@ -130,6 +130,14 @@ class Oracle:
         L.orc_route_top_k.restype = None
         L.orc_route_top_k.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t, C.c_int,
                                       C.POINTER(C.c_int32), C.POINTER(C.c_float)]
+        L.orc_postreq_sample_batch.restype = None
+        L.orc_postreq_sample_batch.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t, C.c_float,
+                                               C.c_float, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_int32)]
+        L.orc_postreq_apply_penalties.restype = None
+        L.orc_postreq_apply_penalties.argtypes = [C.POINTER(C.c_float), C.c_int, C.POINTER(C.c_int32), C.c_int,
+                                                  C.c_float, C.c_int]
+        L.orc_postreq_grammar_mask.restype = None
+        L.orc_postreq_grammar_mask.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int]
         L.orc_random_f32.restype = C.c_float
         L.orc_random_f32.argtypes = [C.POINTER(C.c_uint64)]
         L.orc_expf_range.restype = None
@@ -182,6 +190,32 @@ class Oracle:
         w = np.empty((T, top_k), np.float32)
         self.lib.orc_route_top_k(_ptr(x, C.c_float), T, E, E, top_k, _ptr(ids, C.c_int32), _ptr(w, C.c_float))
         return ids, w
+
+    def postreq_sample(self, logits: np.ndarray, temperature: float, top_p: float, top_k: int, r: np.ndarray):
+        """pipeline_stages.c:103-189 on every row with uniforms r: (ids, the
+        rows as the reference leaves them)."""
+        x = np.array(logits, dtype=np.float32, copy=True, order="C")
+        B, V = x.shape
+        r = np.ascontiguousarray(r, dtype=np.float32)
+        ids = np.empty(B, np.int32)
+        self.lib.orc_postreq_sample_batch(_ptr(x, C.c_float), B, V, V, temperature, top_p, top_k, _ptr(r, C.c_float),
+                                          _ptr(ids, C.c_int32))
+        return ids, x
+
+    def postreq_penalties(self, logits: np.ndarray, history: np.ndarray, penalty: float, window: int):
+        x = np.array(logits, dtype=np.float32, copy=True, order="C")
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        for b in range(x.shape[0]):
+            self.lib.orc_postreq_apply_penalties(x[b].ctypes.data_as(C.POINTER(C.c_float)), x.shape[1],
+                                                 h[b].ctypes.data_as(C.POINTER(C.c_int32)), h.shape[1], penalty,
+                                                 window)
+        return x
+
+    def postreq_grammar(self, logits: np.ndarray, states) -> np.ndarray:
+        x = np.array(logits, dtype=np.float32, copy=True, order="C")
+        for b in range(x.shape[0]):
+            self.lib.orc_postreq_grammar_mask(x[b].ctypes.data_as(C.POINTER(C.c_float)), x.shape[1], int(states[b]))
+        return x
 
     def expf(self, x: np.ndarray) -> np.ndarray:
         """glibc expf on an arbitrary float32 array (via contiguous bit ranges)."""
@@ -269,6 +303,28 @@ class RoutingEntry(C.Structure):
     _fields_ = [("expert_id", C.c_int32), ("weight", C.c_float)]
 
 
+class PostreqParams(C.Structure):
+    """aether_sampling_params_t (reference include/pipeline_stages.h:13-20)."""
+
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int),
+                ("repetition_penalty", C.c_float), ("repetition_window", C.c_int),
+                ("grammar_enforce_json", C.c_bool)]
+
+
+LIBC = C.CDLL(None)
+LIBC.rand.restype = C.c_int
+LIBC.srand.argtypes = [C.c_uint]
+RAND_MAX = 2147483647
+
+
+def rand_uniforms(seed: int, n: int) -> np.ndarray:
+    """The uniforms aether_postreq_sample draws (pipeline_stages.c:180):
+    (float)rand() / (float)RAND_MAX after srand(seed), from this process's C
+    library, the one the reference build links."""
+    LIBC.srand(seed)
+    return np.array([np.float32(LIBC.rand()) / np.float32(RAND_MAX) for _ in range(n)], np.float32)
+
+
 class RefAux:
     """The reference's router and pipeline samplers themselves
     (oracle/_ref/libaux_ref.so: src/sparsity.c, src/pipeline_stages.c)."""
@@ -279,6 +335,13 @@ class RefAux:
         self.lib = C.CDLL(path)
         self.lib.aether_route_top_k.restype = None
         self.lib.aether_route_top_k.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.POINTER(RoutingEntry)]
+        for f in ("aether_postreq_apply_penalties", "aether_postreq_grammar_mask"):
+            getattr(self.lib, f).restype = None
+        self.lib.aether_postreq_apply_penalties.argtypes = [C.POINTER(C.c_float), C.c_int, C.POINTER(C.c_int32),
+                                                            C.c_int, C.c_float, C.c_int]
+        self.lib.aether_postreq_grammar_mask.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int]
+        self.lib.aether_postreq_sample.restype = C.c_int32
+        self.lib.aether_postreq_sample.argtypes = [C.POINTER(C.c_float), C.c_int, C.POINTER(PostreqParams)]
         self.lib.ref_route_batch.restype = None
         self.lib.ref_route_batch.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t, C.c_int,
                                              C.c_void_p, C.c_int]
@@ -307,3 +370,27 @@ class RefAux:
         out = np.empty((T, top_k, 2), np.int32)
         self.lib.ref_route_batch(x.ctypes.data_as(C.POINTER(C.c_float)), T, E, E, top_k, out.ctypes.data, nthreads)
         return out[:, :, 0].copy(), out[:, :, 1].copy().view(np.float32)
+
+    def postreq_sample(self, logits: np.ndarray, params: PostreqParams, seed: int):
+        """The reference's aether_postreq_sample on every row, after
+        srand(seed) (it draws rand() itself): (ids, rows after the calls)."""
+        x = np.array(logits, dtype=np.float32, copy=True, order="C")
+        LIBC.srand(seed)
+        ids = np.array([self.lib.aether_postreq_sample(x[b].ctypes.data_as(C.POINTER(C.c_float)), x.shape[1],
+                                                       C.byref(params)) for b in range(x.shape[0])], np.int32)
+        return ids, x
+
+    def postreq_penalties(self, logits: np.ndarray, history: np.ndarray, penalty: float, window: int):
+        x = np.array(logits, dtype=np.float32, copy=True, order="C")
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        for b in range(x.shape[0]):
+            self.lib.aether_postreq_apply_penalties(x[b].ctypes.data_as(C.POINTER(C.c_float)), x.shape[1],
+                                                    h[b].ctypes.data_as(C.POINTER(C.c_int32)), h.shape[1], penalty,
+                                                    window)
+        return x
+
+    def postreq_grammar(self, logits: np.ndarray, states) -> np.ndarray:
+        x = np.array(logits, dtype=np.float32, copy=True, order="C")
+        for b in range(x.shape[0]):
+            self.lib.aether_postreq_grammar_mask(x[b].ctypes.data_as(C.POINTER(C.c_float)), x.shape[1], int(states[b]))
+        return x
