@@ -813,6 +813,90 @@ def run_postreq(args):
         "gpu_launches": args.steps}), flush=True)
 
 
+def run_lmhead(args):
+    """The LM head feeding the sampler (src/engine.c:377-387): bf16 output
+    weights 152,064 x 4096 (1.25 GB, read from HBM every call), hidden states
+    N(0, 1), the batch1024 sampling parameters, history NULL as the engine
+    passes it; one token (the engine's decode step) and eight.  value =
+    tokens/s through noel_lmhead_sample with inputs resident on the GPU; the
+    roofline is the weights read once per call.  The reference (its own
+    noel_gemv_quantized on the host cores, then noel_sampler_sample) is timed
+    on one token and its logits and token compared with the GPU's."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import torch
+
+    from noel_b200 import sampler as S
+    from noel_b200.workloads import WORKLOADS, row_states
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    V, D = 152064, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    w = (torch.randn(V, D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    cfgkw = WORKLOADS["batch1024"].config_kwargs()
+    cfg = S.make_config(**cfgkw)
+    peak, peak_kind = measured_peak()
+    stream = torch.cuda.current_stream(dev)
+    for B in (1, 8):
+        x = torch.randn(B, D, device=dev, generator=g)
+        rng = torch.from_numpy(row_states(3, np.arange(B)).view(np.int64).copy()).to(dev)
+        logits = torch.empty(B, V, device=dev)
+        ids = torch.empty(B, dtype=torch.int32, device=dev)
+
+        def step():
+            S._check(S.lib().noel_lmhead_sample(S.C.byref(cfg), w.data_ptr(), S.HEAD_BF16, D, x.data_ptr(), D, B, D,
+                                                V, None, 0, 0, rng.data_ptr(), ids.data_ptr(), None,
+                                                logits.data_ptr(), S.C.c_void_p(stream.cuda_stream)))
+
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        wbytes = V * D * 2
+        line = {"metric": f"tokens/s, LM head {V} x {D} bf16 + sampler, {B} token(s) per call",
+                "value": B / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": args.steps,
+                "higher_is_better": True, "dtype": "bf16 weights, f32 accumulate", "data": "synthetic",
+                "config": {"workload": "lmhead", "batch": B, "hidden": D, "vocab": V, **cfgkw},
+                "roofline": {"bound": "hbm", "achieved": wbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": wbytes / (ms / 1e3) / 1e9 / peak, "bytes_per_launch": wbytes,
+                             "kernel": "lmhead_gemv_kernel + the sampler", "peak_source": f"{peak_kind} hbm_gbs"},
+                "gpu_launches": 3 * args.steps}
+        if B == 1 and not args.no_cpu:
+            from oracle.oracle import RefAux, RefSampler, make_config
+
+            if RefAux.available() and RefSampler.available():
+                wh = w.view(torch.int16).cpu().numpy().view(np.uint16)
+                xh = x.cpu().numpy()
+                aux = RefAux()
+                t0 = time.perf_counter()
+                ref_logits = aux.gemv(wh, 30, xh)
+                gemv_s = time.perf_counter() - t0
+                rng0 = row_states(3, np.arange(1))
+                t0 = time.perf_counter()
+                rid = RefSampler().sample_batch(make_config(**cfgkw), ref_logits, rng=rng0, nthreads=1).ids
+                samp_s = time.perf_counter() - t0
+                # the GPU on the same token from the same state
+                rng.copy_(torch.from_numpy(rng0.view(np.int64).copy()).to(dev))
+                step()
+                torch.cuda.synchronize()
+                same = np.array_equal(logits.cpu().numpy().view(np.uint32), ref_logits.view(np.uint32))
+                line["cpu_baseline"] = {"value": 1.0 / (gemv_s + samp_s), "unit": "tokens/s", "cores": os.cpu_count(),
+                                        "kind": "reference",
+                                        "sample": "one token: noel_gemv_quantized (BF16, all host threads) then "
+                                                  "noel_sampler_sample (one thread)",
+                                        "gemv_ms": gemv_s * 1e3, "sample_ms": samp_s * 1e3}
+                line["parity"] = {"logits_bit_exact": bool(same), "ids_equal": bool(ids.cpu().numpy()[0] == rid[0])}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -836,6 +920,8 @@ def main():
         run_router(args)
     elif args.workload == "postreq":
         run_postreq(args)
+    elif args.workload == "lmhead":
+        run_lmhead(args)
     else:
         run_ours(args)
 

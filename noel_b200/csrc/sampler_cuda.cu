@@ -21,9 +21,11 @@
 #include <mutex>
 #include <vector>
 
+#include "noel_lmhead.h"
 #include "noel_postreq.h"
 #include "noel_router.h"
 #include "noel_sampler_cuda.h"
+#include "lmhead.cuh"
 #include "postreq.cuh"
 #include "router.cuh"
 #include "sampler_stream.cuh"
@@ -950,6 +952,71 @@ extern "C" int32_t noel_postreq_sample(float *logits, int vocab_size, const noel
     if (step() != NOEL_OK) return 0;
     ok();
     return *st.h_id;
+}
+
+/* ------------------------------------------------ LM head -> sampler */
+namespace {
+template <int WT, int NB>
+int head_launch_nb(DeviceCtx *c, const HeadArgs &h, cudaStream_t s) {
+    const int grid = (h.rows + kHeadThreads - 1) / kHeadThreads;
+    const int r = set_smem(c, (const void *)lmhead_gemv_kernel<WT, NB>, head_smem_bytes());
+    if (r) return r;
+    lmhead_gemv_kernel<WT, NB><<<grid, kHeadThreads, head_smem_bytes(), s>>>(h);
+    CUDA_TRY(cudaGetLastError());
+    return NOEL_OK;
+}
+template <int WT>
+int head_launch(DeviceCtx *c, const HeadArgs &h, int nb, cudaStream_t s) {
+    switch (nb) {
+        case 8: return head_launch_nb<WT, 8>(c, h, s);
+        case 4: return head_launch_nb<WT, 4>(c, h, s);
+        case 2: return head_launch_nb<WT, 2>(c, h, s);
+        default: return head_launch_nb<WT, 1>(c, h, s);
+    }
+}
+}  // namespace
+
+extern "C" int noel_lmhead_sample(const noel_sampler_config_t *cfg, const void *d_weight, int weight_type,
+                                  size_t ldw, const float *d_hidden, size_t ldh, int batch, int hidden_dim, int vocab,
+                                  const int32_t *d_history, int history_len, size_t hld, uint64_t *d_rng,
+                                  int32_t *d_ids, float *d_probs, float *d_logits, void *stream) {
+    if (!cfg || !d_weight || !d_hidden || !d_logits) return fail(NOEL_ERR_INVALID_ARG, "cfg, weight, hidden and logits are required");
+    if (weight_type != NOEL_HEAD_F32 && weight_type != NOEL_HEAD_F16 && weight_type != NOEL_HEAD_BF16)
+        return fail(NOEL_ERR_UNSUPPORTED, "weight type %d (F32 0, F16 1, BF16 30)", weight_type);
+    if (batch < 0 || vocab <= 0 || hidden_dim <= 0) return fail(NOEL_ERR_INVALID_ARG, "batch / vocab / hidden_dim");
+    if (hidden_dim % 8) return fail(NOEL_ERR_UNSUPPORTED, "hidden_dim %d is not a multiple of 8", hidden_dim);
+    if (ldw < (size_t)hidden_dim || ldw % 8 || ldh < (size_t)hidden_dim || ldh % 4)
+        return fail(NOEL_ERR_INVALID_ARG, "ldw %zu (multiple of 8) / ldh %zu (multiple of 4)", ldw, ldh);
+    if ((reinterpret_cast<uintptr_t>(d_weight) & 15) || (reinterpret_cast<uintptr_t>(d_hidden) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_logits) & 3))
+        return fail(NOEL_ERR_INVALID_ARG, "weight and hidden must be 16-byte aligned");
+    if (batch == 0) return ok();
+    DeviceCtx *c = nullptr;
+    int r = device_ctx(&c);
+    if (r) return r;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int t0 = 0; t0 < batch;) {
+        const int left = batch - t0;
+        const int nb = left >= 8 ? 8 : (left >= 4 ? 4 : (left >= 2 ? 2 : 1));
+        HeadArgs h{};
+        h.w = d_weight;
+        h.ldw = (int64_t)ldw;
+        h.x = d_hidden + (size_t)t0 * ldh;
+        h.ldx = (int64_t)ldh;
+        h.rows = vocab;
+        h.cols = hidden_dim;
+        h.y = d_logits + (size_t)t0 * (size_t)vocab;
+        h.ldy = vocab;
+        r = weight_type == NOEL_HEAD_F32 ? head_launch<kHeadF32>(c, h, nb, s)
+            : weight_type == NOEL_HEAD_F16 ? head_launch<kHeadF16>(c, h, nb, s)
+                                           : head_launch<kHeadBF16>(c, h, nb, s);
+        if (r) return r;
+        t0 += nb;
+    }
+    noel_sample_extras_t ex{};
+    ex.d_probs = d_probs;
+    return sample_batch(cfg, d_logits, NOEL_DTYPE_F32, batch, vocab, (size_t)vocab, d_history, history_len, hld,
+                        d_rng, d_ids, &ex, s);
 }
 
 extern "C" int noel_moe_route_top_k(const float *d_gate_logits, int n_tokens, int n_experts, size_t ld, int top_k,

@@ -126,6 +126,10 @@ def lib() -> C.CDLL:
                                                   C.c_void_p]
     L.noel_postreq_sample.restype = C.c_int32
     L.noel_postreq_sample.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+    L.noel_lmhead_sample.restype = C.c_int
+    L.noel_lmhead_sample.argtypes = [C.POINTER(SamplerConfig), C.c_void_p, C.c_int, C.c_size_t, C.c_void_p,
+                                     C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_size_t,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
     L.noel_moe_route_top_k.restype = C.c_int
     L.noel_moe_route_top_k.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_int, C.c_void_p, C.c_void_p]
     L.noel_sampler_cuda_last_error.restype = C.c_int
@@ -408,3 +412,33 @@ def postreq_sample(logits, params: PostreqParams) -> int:
     if st != 0:
         _check(st)
     return int(r)
+
+
+HEAD_F32, HEAD_F16, HEAD_BF16 = 0, 1, 30
+
+
+def lmhead_sample(weight, hidden, rng, cfg: SamplerConfig, history=None, probs: bool = False):
+    """The LM head then the sampler (include/noel_lmhead.h): weight [V, D]
+    CUDA float32 / float16 / bfloat16 (unit column stride), hidden [B, D]
+    CUDA float32, rng [B, 2] int64 advanced in place, history [B, H] int32 or
+    None.  Returns (ids [B] int32, logits [B, V] float32, probs or None)."""
+    import torch
+
+    wt = {torch.float32: HEAD_F32, torch.float16: HEAD_F16, torch.bfloat16: HEAD_BF16}[weight.dtype]
+    assert weight.is_cuda and hidden.is_cuda and hidden.dtype == torch.float32
+    V, D = weight.shape
+    B = hidden.shape[0]
+    dev = weight.device
+    logits = torch.empty(B, V, dtype=torch.float32, device=dev)
+    ids = torch.empty(B, dtype=torch.int32, device=dev)
+    pr = torch.empty(B, dtype=torch.float32, device=dev) if probs else None
+    if history is not None:
+        hp, H, hld = history.data_ptr(), history.shape[1], history.stride(0)
+    else:
+        hp, H, hld = None, 0, 0
+    s = torch.cuda.current_stream(dev)
+    _check(lib().noel_lmhead_sample(C.byref(cfg), weight.data_ptr(), wt, weight.stride(0), hidden.data_ptr(),
+                                    hidden.stride(0), B, D, V, hp, H, hld, rng.data_ptr(), ids.data_ptr(),
+                                    pr.data_ptr() if pr is not None else None, logits.data_ptr(),
+                                    C.c_void_p(s.cuda_stream)))
+    return ids, logits, pr

@@ -1,7 +1,8 @@
 /*
  * Oracle for the paths next to the sampler: CPU restatements of the
- * reference's MoE router (Sain-Kai/noel src/sparsity.c:46-79) and of the
- * pipeline's sibling sampler (src/pipeline_stages.c:64-189), used ONLY as
+ * reference's MoE router (Sain-Kai/noel src/sparsity.c:46-79), of the
+ * pipeline's sibling sampler (src/pipeline_stages.c:64-189) and of its
+ * LM-head GEMV for unquantised rows (src/dequant.c:412-470), used ONLY as
  * checkers by tests/ and bench.py's CPU leg.  Nothing in the shipped library
  * links, loads or calls this code.
  *
@@ -9,11 +10,12 @@
  * router (tests/test_engine.c:128-142) and against the reference's own
  * sparsity.c and pipeline_stages.c, compiled from their sources into
  * oracle/_ref/libaux_ref.so by oracle/Makefile, on seeded inputs
- * (tests/test_router.py, tests/test_postreq.py).
+ * (tests/test_router.py, tests/test_postreq.py, tests/test_lmhead.py).
  */
 #include <math.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <string.h>
 
 /* sparsity.c:46-79 for tokens t in [0, T): logits row t at logits + t * ld;
  * ids / weights [T][top_k]. */
@@ -139,4 +141,64 @@ int32_t orc_postreq_sample(float *logits, int V, float T, float top_p, int top_k
 void orc_postreq_sample_batch(float *logits, int B, int V, size_t ld, float T, float top_p, int top_k, const float *r,
                               int32_t *ids) {
     for (int b = 0; b < B; ++b) ids[b] = orc_postreq_sample(logits + (size_t)b * ld, V, T, top_p, top_k, r[b]);
+}
+
+/* ------------------------------------------------------------------------ */
+/* LM-head GEMV (src/dequant.c:412-470) for F32 (type 0), F16 (1), BF16 (30) */
+
+static float orc_half(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 31u, m = h & 1023u;
+    uint32_t f;
+    if (e == 0u) {
+        if (m == 0u) f = sign;
+        else { /* subnormal half: normalise */
+            int k = -1;
+            uint32_t mm = m;
+            do { mm <<= 1; ++k; } while (!(mm & 1024u));
+            f = sign | ((uint32_t)(112 - k) << 23) | ((mm & 1023u) << 13);
+        }
+    } else if (e == 31u) {
+        f = sign | 0x7F800000u | (m << 13);
+    } else {
+        f = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    float r;
+    memcpy(&r, &f, 4);
+    return r;
+}
+
+static float orc_elem(int type, const void *row, int j) {
+    if (type == 0) return ((const float *)row)[j];
+    const uint16_t h = ((const uint16_t *)row)[j];
+    if (type == 30) {
+        const uint32_t f = (uint32_t)h << 16;
+        float r;
+        memcpy(&r, &f, 4);
+        return r;
+    }
+    return orc_half(h);
+}
+
+/* y[b][r] for rows r < rows, tokens b < B, cols a multiple of 8: eight fused
+ * multiply-add accumulators over blocks of eight columns, combined as
+ * ((a0 + a4) + (a1 + a5)) + ((a2 + a6) + (a3 + a7)) (dequant.c:437-452).
+ * The reference's scalar loop over a ragged tail (:454-456) is left to its
+ * compiler's scheduling (it matches neither one fused multiply-add per
+ * column nor a multiply and an add), so other widths are not restated. */
+void orc_gemv(int type, const void *W, size_t ldw, const float *x, size_t ldx, int B, int rows, int cols, float *y,
+              size_t ldy) {
+    const size_t es = type == 0 ? 4 : 2;
+    for (int b = 0; b < B; ++b) {
+        const float *xb = x + (size_t)b * ldx;
+        for (int r = 0; r < rows; ++r) {
+            const void *row = (const char *)W + (size_t)r * ldw * es;
+            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int j = 0;
+            for (; j + 8 <= cols; j += 8)
+                for (int k = 0; k < 8; ++k) a[k] = fmaf(orc_elem(type, row, j + k), xb[j + k], a[k]);
+            float s0 = a[0] + a[4], s1 = a[1] + a[5], s2 = a[2] + a[6], s3 = a[3] + a[7];
+            const float dot = (s0 + s1) + (s2 + s3);
+            y[(size_t)b * ldy + r] = dot;
+        }
+    }
 }

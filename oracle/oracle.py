@@ -138,6 +138,9 @@ class Oracle:
                                                   C.c_float, C.c_int]
         L.orc_postreq_grammar_mask.restype = None
         L.orc_postreq_grammar_mask.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int]
+        L.orc_gemv.restype = None
+        L.orc_gemv.argtypes = [C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_float), C.c_size_t, C.c_int, C.c_int,
+                               C.c_int, C.POINTER(C.c_float), C.c_size_t]
         L.orc_random_f32.restype = C.c_float
         L.orc_random_f32.argtypes = [C.POINTER(C.c_uint64)]
         L.orc_expf_range.restype = None
@@ -216,6 +219,17 @@ class Oracle:
         for b in range(x.shape[0]):
             self.lib.orc_postreq_grammar_mask(x[b].ctypes.data_as(C.POINTER(C.c_float)), x.shape[1], int(states[b]))
         return x
+
+    def gemv(self, weight: np.ndarray, wtype: int, x: np.ndarray) -> np.ndarray:
+        """dequant.c:412-470 restated: logits [B, rows] of weight [rows, cols]
+        (float32, or uint16 bf16 / f16 bits for wtype 30 / 1) and x [B, cols]."""
+        w = np.ascontiguousarray(weight)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, cols = w.shape
+        B = x.shape[0]
+        y = np.empty((B, rows), np.float32)
+        self.lib.orc_gemv(wtype, w.ctypes.data, cols, _ptr(x, C.c_float), cols, B, rows, cols, _ptr(y, C.c_float), rows)
+        return y
 
     def expf(self, x: np.ndarray) -> np.ndarray:
         """glibc expf on an arbitrary float32 array (via contiguous bit ranges)."""
@@ -342,6 +356,9 @@ class RefAux:
         self.lib.aether_postreq_grammar_mask.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int]
         self.lib.aether_postreq_sample.restype = C.c_int32
         self.lib.aether_postreq_sample.argtypes = [C.POINTER(C.c_float), C.c_int, C.POINTER(PostreqParams)]
+        self.lib.noel_gemv_quantized.restype = None
+        self.lib.noel_gemv_quantized.argtypes = [C.c_int, C.POINTER(C.c_float), C.c_void_p, C.POINTER(C.c_float),
+                                                 C.c_int, C.c_int, C.c_int]
         self.lib.ref_route_batch.restype = None
         self.lib.ref_route_batch.argtypes = [C.POINTER(C.c_float), C.c_int, C.c_int, C.c_size_t, C.c_int,
                                              C.c_void_p, C.c_int]
@@ -394,3 +411,15 @@ class RefAux:
         for b in range(x.shape[0]):
             self.lib.aether_postreq_grammar_mask(x[b].ctypes.data_as(C.POINTER(C.c_float)), x.shape[1], int(states[b]))
         return x
+
+    def gemv(self, weight: np.ndarray, wtype: int, x: np.ndarray, nthreads: int = 0) -> np.ndarray:
+        """The reference's noel_gemv_quantized (dequant.c:412) for each row of x."""
+        w = np.ascontiguousarray(weight)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, cols = w.shape
+        y = np.empty((x.shape[0], rows), np.float32)
+        for b in range(x.shape[0]):
+            self.lib.noel_gemv_quantized(wtype, y[b].ctypes.data_as(C.POINTER(C.c_float)), w.ctypes.data,
+                                         x[b].ctypes.data_as(C.POINTER(C.c_float)), rows, cols,
+                                         nthreads or os.cpu_count())
+        return y
