@@ -72,14 +72,6 @@ __host__ __device__ constexpr size_t head_smem_bytes() {
     return (size_t)kHeadStages * (kHeadThreads * kHeadPitch + kHeadXMax * 4);
 }
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 /* The CTA's 128 rows stream through shared memory in tiles of 128 bytes of
  * every row (64 columns of a 2-byte type, 32 of F32): each warp load covers
  * four rows x 128 contiguous bytes, kHeadStages tiles are in flight, and the

@@ -11,6 +11,7 @@
  */
 #include <cuda_runtime.h>
 
+#include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -266,6 +267,26 @@ struct ShardOut {
  * K' = 128 (top-k 57..120) half is as safe: a warp's share of the 128 best
  * stays near 32.  Keeping all K' everywhere makes compactions frequent and
  * costs more than it saves. */
+/* Rank r of the single-pass warm-up's starting filter, the r-th largest of
+ * a uniform sample of s of a row's v elements: the smallest r for which the
+ * row's K' largest put r or more elements in the sample with probability at
+ * most 1e-9 (the Poisson tail of mean K' s / v, which bounds the sample's
+ * hypergeometric count from above).  Fewer than r of them in the sample
+ * leave K' row elements above the filter; otherwise the row end finds fewer
+ * than K' passed and the row goes to the two-pass kernel.  K' when the
+ * sample is the whole row (the filter is then proved). */
+int warm_rank(int kprime, long long s, long long v) {
+    if (s >= v) return kprime;
+    const double x = (double)kprime * (double)s / (double)v;
+    double p = exp(-x), cdf = 0.0;  // p = P(count = r - 1)
+    for (int r = 1; r < kprime; ++r) {
+        cdf += p;
+        if (1.0 - cdf <= 1e-9) return r;
+        p *= x / r;
+    }
+    return kprime;
+}
+
 int warp_keep(int kprime) { return kprime <= 32 ? kprime : (kprime <= 64 ? 3 * kprime / 4 : kprime / 2); }
 
 /* Entries of a warp's candidate buffer: a compaction sorts the buffer and
@@ -439,6 +460,7 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
             wide = B <= 2 * c->sms;
             const int u = (dtype == NOEL_DTYPE_F32 ? 2 : 1) * (wide ? 4 : 1);  // vectors per lane and batch
             a.qcap = 32 * u > kQueueCap ? 32 * u : kQueueCap;
+            if (mode == kTopK) a.warm_rank = warm_rank(a.kprime, (long long)nw * 32 * 16 * (wide ? 4 : 1), V);
             /* the row-end union: every warp's whole buffer for K' > 32, each
              * warp's best kw below */
             a.ucap = mode == kTopK && a.kprime <= 32 ? nw * a.kw : nw * a.cap;

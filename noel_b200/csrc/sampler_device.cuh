@@ -59,6 +59,7 @@ struct SampleArgs {
     float top_p;
     int top_k;
     int kprime;                 // kept-set size for top-k
+    int warm_rank;              // rank of the single-pass warm-up's starting filter (0: K')
     int kw;                     // entries a warp keeps when it compacts (single-pass kernel)
     int cap;                    // candidate buffer entries
     int hcap;                   // history hash-table slots (single-pass kernel)
@@ -436,6 +437,15 @@ __device__ __forceinline__ V8 ld_stream(const V8 *p) {
         : "l"(p));
     return r;
 }
+
+/* 16-byte global -> shared copies that bypass the registers (and L1) */
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 /* Row geometry: scalar head until 32-byte alignment, vector body, scalar tail. */
 struct RowGeom {

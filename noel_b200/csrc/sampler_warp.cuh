@@ -482,17 +482,32 @@ __device__ __noinline__ uint64_t greedy_take(const SampleArgs &a, uint32_t id0, 
     return ((uint64_t)__float_as_uint(gx) << 32) | gid;
 }
 
-/* Block warm-up on every warp's first batch (all threads of the block): the
- * smallest raw lane maximum of a warp has 32 of the warp's raw elements above
- * it and becomes the warp's own threshold (an exclusion threshold checked at
- * the row end, so it needs no proof); the second largest of those bounds a
- * two-level histogram (9 key bits, then the next 9 inside the chosen bin) of
- * the larger elements, penalised, whose bin holding the K'-th largest gives
- * the row's starting threshold.  The penalty only lowers values, so only
- * elements whose raw value reaches the histogram are looked up.  Returns the
- * warp's own threshold. */
+/* Vector of the row's body that warm-up sample slot (warp, u, lane) reads:
+ * the block's NW * 32 * U slots spread evenly over the body (a uniform
+ * sample of the row whatever the order of its ids), or the whole body when
+ * it is shorter; -1 for a slot past it. */
+template <int U>
+__device__ __forceinline__ int warm_vec(int nvec, int warp, int u, int lane) {
+    constexpr int NS = kRowWarps * 32 * U;
+    const int j = (warp * U + u) * 32 + lane;
+    if (nvec >= NS) return (int)(((long long)j * nvec) / NS);
+    return j < nvec ? j : -1;
+}
+
+/* Block warm-up on the row's sample (all threads of the block; slot (u,
+ * lane) of each warp's queue holds the vector warm_vec names): the smallest
+ * raw lane maximum of a warp has 32 raw elements above it and becomes the
+ * warp's own threshold (an exclusion threshold checked at the row end, so it
+ * needs no proof); the second largest of those bounds a two-level histogram
+ * (9 key bits, then the next 9 inside the chosen bin) of the larger sample
+ * elements, penalised, whose bin holding the r-th largest (r = warm_rank)
+ * gives the row's starting filter.  With r < K' the filter is a bet, not a
+ * proof: it drops elements below it, and the row end sends the row to the
+ * two-pass kernel when fewer than K' elements passed it.  The penalty only
+ * lowers values, so only elements whose raw value reaches the histogram are
+ * looked up.  Returns the warp's own threshold. */
 template <typename T, int UX>
-__device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, int head, int v0, int v1) {
+__device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, int head, int nvec) {
     using F = Fmt<T>;
     constexpr int NT = kRowThreads, NW = kRowWarps;
     constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U * UX, NE = U * VEC;
@@ -501,8 +516,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
     float xw[NE];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-        const int vi = v0 + u * 32 + lane;
-        if (vi < v1) {
+        if (warm_vec<U>(nvec, warp, u, lane) >= 0) {
             F::unpack(ld_vec(L.q + u * 32 + lane), xw + u * VEC);
         } else {
 #pragma unroll
@@ -543,7 +557,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         const int u = e / VEC, j = e - (e / VEC) * VEC;
         float x = F::scalar(wq + u * 32 + lane, j);
         float pv;
-        if (a.penalty && hs_find(L.hs, (uint32_t)(head + (v0 + u * 32 + lane) * VEC + j), pv)) x = pv;
+        if (a.penalty && hs_find(L.hs, (uint32_t)(head + warm_vec<U>(nvec, warp, u, lane) * VEC + j), pv)) x = pv;
         return x;
     };
     auto reach = [&](uint32_t floor_key) -> uint64_t {
@@ -564,7 +578,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         if (a.penalty) {  // only what reaches the histogram needs its penalised value
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const uint32_t id0 = (uint32_t)(head + (v0 + u * 32 + lane) * VEC);
+                const uint32_t id0 = (uint32_t)(head + warm_vec<U>(nvec, warp, u, lane) * VEC);
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) {
                     float &xv = xw[u * VEC + j];
@@ -581,7 +595,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
     }
     __syncthreads();
     int need;
-    const int wb1 = block_find_bin_desc<NT>(L.area, a.kprime, rs.w, rs.res, &need);
+    const int wb1 = block_find_bin_desc<NT>(L.area, a.warm_rank > 0 ? a.warm_rank : a.kprime, rs.w, rs.res, &need);
     if (wb1 >= 0) {
         uint32_t *h2 = L.area + kWarpBins;
         for (int i = tid; i < kWarpBins; i += NT) h2[i] = 0u;
@@ -604,7 +618,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         const int wb2 = block_find_bin_desc<NT>(h2, need, rs.w, rs.res, &need2);
         if (tid == 0 && wb2 >= 0) {
             const uint32_t key = ((uint32_t)wb1 << 23) | ((uint32_t)wb2 << 14);
-            rs.tsh = (unsigned long long)key << 32;  // K' first-batch elements beat it
+            rs.tsh = (unsigned long long)key << 32;  // r sample elements reach it
         }
         __syncthreads();
     }
@@ -695,7 +709,8 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
      * (a sort of up to NW buffers costs more than those small selections) */
     const bool bsort = MODE == kTopK && a.kprime > 32;
     if (MODE == kTopK) {
-        /* entries below the shared filter cannot make the top K' */
+        /* entries below the shared filter are excluded like every element
+         * the filter dropped while streaming */
         const unsigned long long t2 = rs.tsh;
         if (t2) {
             int wn = 0;
@@ -768,8 +783,9 @@ __device__ __forceinline__ void row_finish(const SampleArgs &a, unsigned long lo
     uint32_t t_last = 0u;
     if (MODE == kTopK && (n > a.kprime || trunc)) {
         /* Every excluded element must rank below the K'-th kept one: the
-         * shared filter guarantees it; a warp's own cut does when the K'-th
-         * kept key beats that warp's final threshold. */
+         * shared filter guarantees it once K' elements passed it (every kept
+         * one did); a warp's own cut does when the K'-th kept key beats that
+         * warp's final threshold. */
         unsigned long long worst = 0ull;
         for (int w = 0; w < NW; ++w) worst = max(worst, rs.taus[w]);
         const unsigned long long T = n < a.kprime ? 0ull
@@ -921,6 +937,25 @@ __global__ void __launch_bounds__(kRowThreads, (RowOcc<MODE, UX>::kCtas))
     const RowSpan span = row_span(a, row);
     const int V = span.V;
     const void *rowp = static_cast<const char *>(a.logits) + (size_t)span.off * F::ES;
+    const RowGeom g = row_geom<T>(rowp, V);
+    const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
+
+    /* top-k: the warm-up sample is copied into each warp's queue (still
+     * empty) while the history table is built */
+    const bool warm = MODE == kTopK && min(g.nvec, NW * 32 * U) * VEC >= 4 * a.kprime;
+    if (warm) {
+        V8 *const q = reinterpret_cast<V8 *>(row_smem) + warp * a.qcap;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int vi = warm_vec<U>(g.nvec, warp, u, lane);
+            if (vi >= 0) {
+                cp_async16(q + u * 32 + lane, vbase + vi);
+                cp_async16(reinterpret_cast<char *>(q + u * 32 + lane) + 16,
+                           reinterpret_cast<const char *>(vbase + vi) + 16);
+            }
+        }
+        cp_async_commit();
+    }
 
     {
         const RowLayout L = row_layout<MODE>(a, warp);
@@ -946,8 +981,6 @@ __global__ void __launch_bounds__(kRowThreads, (RowOcc<MODE, UX>::kCtas))
         __syncthreads();
     }
 
-    const RowGeom g = row_geom<T>(rowp, V);
-    const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
     /* greedy: a quarter of the row per warp; queued modes: batches of 32U
      * vectors handed out by ticket, ticket w first for warp w, the rest taken
      * as warps free up.  Ticket t names batch (t mod 4) * bq + t / 4: the first
@@ -1002,9 +1035,9 @@ __global__ void __launch_bounds__(kRowThreads, (RowOcc<MODE, UX>::kCtas))
         }
     }
 
-    /* first batch of this warp's slice (greedy prefetch, top-k warm-up) */
+    /* greedy: first batch of this warp's slice, prefetched */
     V8 nxt[U];
-    if (MODE != kFullList) {
+    if (MODE == kGreedy) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int vi = v0 + u * 32 + lane;
@@ -1013,14 +1046,10 @@ __global__ void __launch_bounds__(kRowThreads, (RowOcc<MODE, UX>::kCtas))
     }
 
     unsigned long long tau_w = 0ull;
-    if (MODE == kTopK && min(g.nvec, NW * 32 * U) * VEC >= 4 * a.kprime) {
-        /* the first batch goes through this warp's queue, still empty */
-        V8 *const q = reinterpret_cast<V8 *>(row_smem) + warp * a.qcap;
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (v0 + u * 32 + lane < v1) st_vec(q + u * 32 + lane, nxt[u]);
+    if (warm) {
+        cp_async_wait<0>();  // this lane's sample slots have landed
         __syncwarp();
-        tau_w = row_warmup<T, UX>(a, g.head, v0, v1);
+        tau_w = row_warmup<T, UX>(a, g.head, g.nvec);
     }
 
     /* ---- the warp's slice of the vector body ---- */
