@@ -233,9 +233,10 @@ int launch_t(const SampleArgs &a0, int mode, bool block_kernel, bool wide, bool 
     CUDA_TRY(cudaGetLastError());
     if (t_ev_after) CUDA_TRY(cudaEventRecord(t_ev_after, s));
     if (mode != kGreedy) {
-        /* launched as a programmatic dependent of the main kernel: its launch
-         * overlaps the main kernel's last CTAs, and it waits for that grid
-         * (griddepcontrol.wait) before it reads the row list */
+        /* launched as a programmatic dependent of the main kernel, which
+         * allows it at its start: its launch overlaps the main kernel's last
+         * CTAs, and it waits for that grid (griddepcontrol.wait) before it
+         * reads the row list */
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(a0.nslots);
         lc.blockDim = dim3(kExactThreads);

@@ -438,6 +438,15 @@ __device__ __forceinline__ V8 ld_stream(const V8 *p) {
     return r;
 }
 
+/* Called at the start of every kernel the two-pass kernel follows (a
+ * programmatic dependent launch): once every CTA of this grid has called it,
+ * the dependent grid may be scheduled, and its launch overlaps this grid's
+ * last CTAs.  The dependent still waits (griddepcontrol.wait) until this
+ * grid has finished and its writes are visible. */
+__device__ __forceinline__ void allow_dependent_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 /* 16-byte global -> shared copies that bypass the registers (and L1) */
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)

@@ -52,6 +52,7 @@ __device__ __forceinline__ void list_exact_row(const SampleArgs &a, int row) {
 /* Every row of the launch for exact_rows_kernel (the rows of a full-list
  * vocab shard whose history and list do not fit the streaming kernel). */
 __global__ void list_all_rows_kernel(const SampleArgs a) {
+    allow_dependent_launch();
     for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < a.batch; r += gridDim.x * blockDim.x) a.exact_list[r] = r;
     if (blockIdx.x == 0 && threadIdx.x == 0) a.counters[0] = a.batch;
 }
@@ -61,6 +62,7 @@ __global__ void list_all_rows_kernel(const SampleArgs a) {
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(const SampleArgs a) {
+    allow_dependent_launch();
     using F = Fmt<T>;
     constexpr int NT = kMainThreads;
     constexpr int VEC = F::VEC, U = F::U, NE = U * VEC;

@@ -1121,6 +1121,7 @@ __device__ void stream_consume(const SampleArgs &a, StreamShared &sh, unsigned c
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kSThreads, 1) stream_rows_kernel(const __grid_constant__ SampleArgs a) {
+    allow_dependent_launch();
     using F = Fmt<T>;
     extern __shared__ __align__(1024) unsigned char stream_smem[];
     __shared__ StreamShared sh;

@@ -928,6 +928,7 @@ struct RowOcc {
 template <typename T, int MODE, int UX>
 __global__ void __launch_bounds__(kRowThreads, (RowOcc<MODE, UX>::kCtas))
     sample_rows_kernel(const __grid_constant__ SampleArgs a) {
+    allow_dependent_launch();
     using F = Fmt<T>;
     constexpr int NT = kRowThreads, NW = kRowWarps;
     constexpr int VEC = WarpFmt<T>::VEC, U = WarpFmt<T>::U * UX, NE = U * VEC;
