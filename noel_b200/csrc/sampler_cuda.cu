@@ -397,6 +397,7 @@ int sample_batch(const noel_sampler_config_t *cfg, const void *logits, int dtype
             block_kernel = true;
             const int cap = pow2_at_least(4 * a.kprime);
             a.cap = cap < 512 ? 512 : (cap > kCapMax ? kCapMax : cap);
+            a.warm_rank = warm_rank(a.kprime, (long long)kMainThreads * 2 * 16, V);  // 8192 sampled elements
         }
     } else if (mode == kFullList) {
         a.cap = 256;

@@ -38,7 +38,7 @@ constexpr uint32_t kFull = 0xFFFFFFFFu;
 enum Mode { kGreedy = 0, kTopK = 1, kFullList = 2 };
 
 /* Flags kept per row in shared memory. */
-enum { kTruncated = 1, kOverflow = 2, kNeedExact = 4 };
+enum { kTruncated = 1, kOverflow = 2, kNeedExact = 4, kWarmBet = 8 };
 
 struct ExpTable {
     const uint32_t *keys, *vals, *offs;

@@ -60,6 +60,46 @@ __global__ void list_all_rows_kernel(const SampleArgs a) {
 /* ====================================================================== */
 /* block-level kernel for large kept sets (k > 120): one CTA per row       */
 
+/* Bin of an NB-bin histogram holding the K-th largest entry, counted from the
+ * top bin down (warp 0, every lane): -1 if the total is below K; *need = how
+ * many of that bin's entries are needed. */
+template <int NB>
+__device__ int warp_find_bin_desc(const uint32_t *h, int K, int *need) {
+    const int lane = threadIdx.x & 31;
+    constexpr int PER = NB / 32;
+    int sum = 0;
+    for (int j = 0; j < PER; ++j) sum += (int)h[NB - 1 - lane * PER - j];
+    const int inc = warp_incl_scan(sum);
+    int bin = -1, nd = 0;
+    if (inc - sum < K && K <= inc) {
+        int cum = inc - sum;
+        for (int j = 0; j < PER; ++j) {
+            const int b = NB - 1 - lane * PER - j;
+            const int c = (int)h[b];
+            if (cum + c >= K) {
+                bin = b;
+                nd = K - cum;
+                break;
+            }
+            cum += c;
+        }
+    }
+    const uint32_t m = __ballot_sync(kFull, bin >= 0);
+    if (!m) return -1;
+    const int src = __ffs(m) - 1;
+    *need = __shfl_sync(kFull, nd, src);
+    return __shfl_sync(kFull, bin, src);
+}
+
+/* Vector of the row's body read by sample slot j of the block kernel's
+ * warm-up: NS slots spread evenly over the body, or the whole body when it is
+ * shorter; -1 for a slot past it. */
+template <int NS>
+__device__ __forceinline__ int block_sample_vec(int j, int nvec) {
+    if (nvec >= NS) return (int)(((long long)j * nvec) / NS);
+    return j < nvec ? j : -1;
+}
+
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(const SampleArgs a) {
     allow_dependent_launch();
@@ -75,6 +115,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
     __shared__ uint32_t s_tau_key, s_tau_id, s_maxkey;
     __shared__ float s_fin_mass;
     __shared__ uint32_t s_gbest_key[NT / 32], s_gbest_id[NT / 32];
+    __shared__ int s_wb1, s_wneed;
 
     const int tid = threadIdx.x, lane = tid & 31;
     const int row = blockIdx.x;
@@ -154,6 +195,82 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
     const int iters = (g.nvec + per_iter - 1) / per_iter;
     const bool warm = (MODE == kTopK) && min(g.nvec, per_iter) * VEC >= 2 * a.kprime;
 
+    /* Warm-up (top-k): a sample of NT * U vectors spread evenly over the row,
+     * penalised; a two-level histogram (11 key bits, then the next 11 inside
+     * the chosen bin) of it gives the floor of the bin holding its r-th
+     * largest (r = warm_rank) as the starting filter.  With r < K' the filter
+     * is a bet: the row end sends the row to the two-pass kernel when fewer
+     * than K' elements passed it. */
+    if (warm) {
+        const int r = a.warm_rank > 0 ? a.warm_rank : a.kprime;
+        float xs[NE];
+        {
+            V8 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int vi = block_sample_vec<NT * U>(u * NT + tid, g.nvec);
+                if (vi >= 0) v[u] = ld_stream(vbase + vi);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int vi = block_sample_vec<NT * U>(u * NT + tid, g.nvec);
+                if (vi >= 0) {
+                    F::unpack(v[u], xs + u * VEC);
+                    if (a.penalty) {
+                        const int id0 = g.head + vi * VEC;
+                        uint32_t bits = hist_bits(hv, id0, VEC);
+                        while (bits) {
+                            const int j = __ffs(bits) - 1;
+                            bits &= bits - 1;
+                            const float pv = __uint_as_float(hv.cnt[hist_rank(hv, id0 + j)]);
+#pragma unroll
+                            for (int jj = 0; jj < VEC; ++jj)
+                                if (jj == j) xs[u * VEC + jj] = pv;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < VEC; ++j) xs[u * VEC + j] = __uint_as_float(0x7FC00000u);  // not counted
+                }
+            }
+        }
+        for (int i = tid; i < kWarmBins; i += NT) whist[i] = 0u;
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < NE; ++e)
+            if (xs[e] == xs[e]) atomicAdd(&whist[ord_key(xs[e]) >> 21], 1u);
+        __syncthreads();
+        if (tid < 32) {
+            int need = 0;
+            const int b1 = warp_find_bin_desc<kWarmBins>(whist, r, &need);
+            if (lane == 0) {
+                s_wb1 = b1;
+                s_wneed = need;
+            }
+        }
+        __syncthreads();
+        const int b1 = s_wb1;
+        if (b1 >= 0) {
+            for (int i = tid; i < kWarmBins; i += NT) whist[i] = 0u;
+            __syncthreads();
+#pragma unroll
+            for (int e = 0; e < NE; ++e)
+                if (xs[e] == xs[e] && (int)(ord_key(xs[e]) >> 21) == b1)
+                    atomicAdd(&whist[(ord_key(xs[e]) >> 10) & (kWarmBins - 1)], 1u);
+            __syncthreads();
+            if (tid < 32) {
+                int need2 = 0;
+                const int b2 = warp_find_bin_desc<kWarmBins>(whist, s_wneed, &need2);
+                if (lane == 0 && b2 >= 0) {
+                    s_tau_key = ((uint32_t)b1 << 21) | ((uint32_t)b2 << 10);  // r sample elements reach it
+                    s_tau_id = 0xFFFFFFFFu;
+                    s_flags |= kTruncated | (r < a.kprime ? kWarmBet : 0);
+                }
+            }
+            __syncthreads();
+        }
+    }
+
     for (int it = 0; it < iters; ++it) {
         float x[NE];
         uint32_t valid = 0u;
@@ -180,7 +297,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
             /* Top-k after the warm-up: the penalty only lowers values, so an
              * element whose raw value is below the current threshold fails
              * the filter either way and needs no history lookup. */
-            const float ptau = (MODE == kTopK && !(warm && it == 0)) ? key_float(s_tau_key) : -INFINITY;
+            const float ptau = MODE == kTopK ? key_float(s_tau_key) : -INFINITY;
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int vi = it * per_iter + u * NT + tid;
@@ -223,35 +340,6 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
         }
 
         /* ---- candidate filter ---- */
-        if (MODE == kTopK && warm && it == 0) {
-            for (int i = tid; i < kWarmBins; i += NT) whist[i] = 0u;
-            __syncthreads();
-#pragma unroll
-            for (int e = 0; e < NE; ++e)
-                if (((valid >> e) & 1u) && x[e] == x[e]) atomicAdd(&whist[ord_key(x[e]) >> 21], 1u);
-            __syncthreads();
-            if (tid < 32) {  // bin holding the K'-th largest, scanning from the top
-                int s = 0;
-                for (int j = 0; j < kWarmBins / 32; ++j) s += (int)whist[kWarmBins - 1 - lane * (kWarmBins / 32) - j];
-                const int inc = warp_incl_scan(s);
-                const int before = inc - s;
-                if (before < a.kprime && a.kprime <= inc) {
-                    int cum = before;
-                    for (int j = 0; j < kWarmBins / 32; ++j) {
-                        const int b = kWarmBins - 1 - lane * (kWarmBins / 32) - j;
-                        cum += (int)whist[b];
-                        if (cum >= a.kprime) {
-                            s_tau_key = (uint32_t)b << 21;
-                            s_tau_id = 0xFFFFFFFFu;
-                            s_flags |= kTruncated;
-                            break;
-                        }
-                    }
-                }
-            }
-            __syncthreads();
-        }
-
         float m_cur = 0.0f;
         if (MODE == kFullList) {
             float lm = -INFINITY;
@@ -422,6 +510,10 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
     }
 
     int n = s_n;
+    if (MODE == kTopK && (s_flags & kWarmBet) && n < a.kprime) {  // the warm-up's bet lost
+        if (tid == 0) list_exact_row(a, row);
+        return;
+    }
     bool trunc = (s_flags & kTruncated) != 0;
     uint32_t t_last = 0u;
     if (MODE == kTopK && (n > a.kprime || trunc)) {

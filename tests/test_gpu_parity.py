@@ -186,22 +186,27 @@ def test_exact_pass_rows_gpu(cuda, oracle):
     assert_parity("ties", g, o)
 
 
-def _warm_sample_vectors(V, f32, wide):
-    """Vector indices the single-pass kernel's warm-up sample reads in a row
-    starting on a 32-byte boundary: 4 warps x 32 lanes x U slots spread
-    evenly over the row's 32-byte vectors."""
-    U = (2 if f32 else 1) * (4 if wide else 1)
-    ns = 4 * 32 * U
+def _warm_sample_vectors(V, f32, wide, block):
+    """Vector indices the warm-up sample reads in a row starting on a 32-byte
+    boundary: the single-pass kernel's 4 warps x 32 lanes x U slots, or the
+    block kernel's (top-k above 120) 256 threads x U slots, spread evenly
+    over the row's 32-byte vectors."""
+    if block:
+        ns = 256 * (4 if f32 else 2)
+    else:
+        ns = 4 * 32 * (2 if f32 else 1) * (4 if wide else 1)
     nvec = V // (8 if f32 else 16)
     return np.arange(ns, dtype=np.int64) * nvec // ns
 
 
-@pytest.mark.parametrize("B,dtype", [(6, "f32"), (300, "f32"), (6, "bf16"), (300, "bf16")])
-def test_warm_filter_bet_lost_gpu(cuda, oracle, B, dtype):
-    """The single-pass kernel starts a top-k row with a filter at a rank
-    below K' of a sample spread over the row.  Rows whose largest elements
-    all lie on the sampled vectors leave fewer than K' elements above it;
-    they must go to the two-pass kernel and still match the oracle."""
+@pytest.mark.parametrize("B,dtype,top_k", [(6, "f32", 40), (300, "f32", 40), (6, "bf16", 40), (300, "bf16", 40),
+                                           (6, "f32", 500), (6, "bf16", 500)])
+def test_warm_filter_bet_lost_gpu(cuda, oracle, B, dtype, top_k):
+    """The single-pass and block kernels start a top-k row with a filter at a
+    rank below K' of a sample spread over the row.  Rows whose largest
+    elements all lie on the sampled vectors leave fewer than K' elements
+    above it; they must go to the two-pass kernel and still match the
+    oracle."""
     from noel_b200.workloads import f32_to_bf16_bits, row_states
 
     V = 32768
@@ -209,18 +214,18 @@ def test_warm_filter_bet_lost_gpu(cuda, oracle, B, dtype):
     g = np.random.Generator(np.random.PCG64(11))
     x = g.standard_normal((B, V)).astype(np.float32)
     vec = 8 if f32 else 16
-    vi = _warm_sample_vectors(V, f32, wide=B <= 296)
+    vi = _warm_sample_vectors(V, f32, wide=B <= 296, block=top_k > 120)
     cols = (vi[:, None] * vec + np.arange(vec)[None, :]).ravel()
     x[:, cols] += 10.0
     hist = np.concatenate([cols[g.integers(0, cols.size, (B, 16))], g.integers(0, V, (B, 16))], axis=1)
     hist = hist.astype(np.int32)
     logits = x if f32 else f32_to_bf16_bits(x)
-    cfgkw = dict(temperature=0.8, top_p=0.95, top_k=40, repetition_penalty=1.3, repetition_window=32, seed=0)
+    cfgkw = dict(temperature=0.8, top_p=0.95, top_k=top_k, repetition_penalty=1.3, repetition_window=32, seed=0)
     st = row_states(5, np.arange(B))
     o = oracle.sample_batch(orc_config(**cfgkw), logits, history=hist, rng=st, n_list=64)
     r = run_gpu(cuda, cfgkw, logits, hist, st)
     assert (r["stats"][:, 3] & 2).all(), "expected every row in the two-pass kernel"
-    assert_parity(f"warm_bet_{dtype}_{B}", r, o)
+    assert_parity(f"warm_bet_{dtype}_{B}_k{top_k}", r, o)
 
 
 def test_single_row_abi_known_answers_gpu(cuda):
