@@ -306,21 +306,33 @@ __device__ __forceinline__ int hist_rank(const HistView &h, int t) {
  * ids in most lanes).  With h.idr, every distinct id's count then becomes its
  * penalised logit (sampler.c:96-100, once per occurrence), computed once per
  * row with the ranks spread over the threads. */
+constexpr int kHistBatch = 8;  // history rounds (and penalised logits) whose loads are issued together
+
 template <int NT, typename T = float>
 __device__ void build_history(const HistView &h, const int32_t *hrow, int first, int H, int V,
                               int *s_w, int id_off = 0, const void *rowp = nullptr, float rep = 1.0f) {
+    constexpr int R = kHistBatch;
     const int W = h.words, G = (W + 7) >> 3;
     for (int i = threadIdx.x; i < W; i += NT) h.bm[i] = 0u;
     __syncthreads();
-    for (int b = first; b < H; b += NT) {  // whole warps per round
-        const int i = b + (int)threadIdx.x;
-        const int g = i < H ? hrow[i] : -1;
-        const bool in = i < H && g >= id_off && g - id_off < V;  // sampler.c:95 (ids of this shard)
-        const int t = g - id_off;
-        const uint32_t wd = in ? (uint32_t)(t >> 5) : 0xFFFFFFFFu;
-        const uint32_t grp = __match_any_sync(0xFFFFFFFFu, wd);
-        const uint32_t bits = __reduce_or_sync(grp, in ? 1u << (t & 31) : 0u);
-        if (in && (int)(threadIdx.x & 31) == __ffs(grp) - 1) atomicOr(&h.bm[wd], bits);
+    for (int b0 = first; b0 < H; b0 += NT * R) {  // R rounds of whole warps, their loads issued together
+        int gv[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = b0 + r * NT + (int)threadIdx.x;
+            gv[r] = i < H ? hrow[i] : -1;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = b0 + r * NT + (int)threadIdx.x;
+            const int g = gv[r];
+            const bool in = i < H && g >= id_off && g - id_off < V;  // sampler.c:95 (ids of this shard)
+            const int t = g - id_off;
+            const uint32_t wd = in ? (uint32_t)(t >> 5) : 0xFFFFFFFFu;
+            const uint32_t grp = __match_any_sync(0xFFFFFFFFu, wd);
+            const uint32_t bits = __reduce_or_sync(grp, in ? 1u << (t & 31) : 0u);
+            if (in && (int)(threadIdx.x & 31) == __ffs(grp) - 1) atomicOr(&h.bm[wd], bits);
+        }
     }
     __syncthreads();
     const int per = (G + NT - 1) / NT;
@@ -342,28 +354,48 @@ __device__ void build_history(const HistView &h, const int32_t *hrow, int first,
     if (threadIdx.x == 0) h.gpre[G] = (uint32_t)total;
     for (int i = threadIdx.x; i < total; i += NT) h.cnt[i] = 0u;
     __syncthreads();
-    for (int b = first; b < H; b += NT) {  // whole warps per round
-        const int i = b + (int)threadIdx.x;
-        const int g = i < H ? hrow[i] : -1;
-        const bool in = i < H && g >= id_off && g - id_off < V;
-        const uint32_t same = __match_any_sync(0xFFFFFFFFu, in ? (uint32_t)(g - id_off) : 0xFFFFFFFFu);
-        /* lanes holding the same id count it once (a skewed window repeats a
-         * few ids in most lanes) */
-        if (in && (int)(threadIdx.x & 31) == __ffs(same) - 1) {
-            const int r = hist_rank(h, g - id_off);
-            const uint32_t before = atomicAdd(&h.cnt[r], (uint32_t)__popc(same));
-            if (h.idr && before == 0u) h.idr[r] = (uint32_t)(g - id_off);  // the first count names the rank
+    for (int b0 = first; b0 < H; b0 += NT * R) {
+        int gv[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = b0 + r * NT + (int)threadIdx.x;
+            gv[r] = i < H ? hrow[i] : -1;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = b0 + r * NT + (int)threadIdx.x;
+            const int g = gv[r];
+            const bool in = i < H && g >= id_off && g - id_off < V;
+            const uint32_t same = __match_any_sync(0xFFFFFFFFu, in ? (uint32_t)(g - id_off) : 0xFFFFFFFFu);
+            /* lanes holding the same id count it once (a skewed window
+             * repeats a few ids in most lanes) */
+            if (in && (int)(threadIdx.x & 31) == __ffs(same) - 1) {
+                const int rk = hist_rank(h, g - id_off);
+                const uint32_t before = atomicAdd(&h.cnt[rk], (uint32_t)__popc(same));
+                if (h.idr && before == 0u) h.idr[rk] = (uint32_t)(g - id_off);  // the first count names the rank
+            }
         }
     }
     __syncthreads();
     if (h.idr) {
         const int total = (int)h.gpre[G];
-        for (int r = threadIdx.x; r < total; r += NT)
-        {
-            const int id = (int)h.idr[r];
-            const float x = sizeof(T) == 4 ? static_cast<const float *>(rowp)[id]  // fp32, or bf16 widened
+        for (int r0 = threadIdx.x; r0 < total; r0 += NT * R) {  // R logits loaded together
+            float xs[R];
+#pragma unroll
+            for (int k = 0; k < R; ++k) {
+                const int r = r0 + k * NT;
+                xs[k] = 0.0f;
+                if (r < total) {
+                    const int id = (int)h.idr[r];
+                    xs[k] = sizeof(T) == 4 ? static_cast<const float *>(rowp)[id]  // fp32, or bf16 widened
                                            : __uint_as_float((uint32_t)static_cast<const uint16_t *>(rowp)[id] << 16);
-            h.cnt[r] = __float_as_uint(apply_penalty(x, h.cnt[r], rep));
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < R; ++k) {
+                const int r = r0 + k * NT;
+                if (r < total) h.cnt[r] = __float_as_uint(apply_penalty(xs[k], h.cnt[r], rep));
+            }
         }
         __syncthreads();
     }
@@ -445,6 +477,12 @@ __device__ __forceinline__ V8 ld_stream(const V8 *p) {
  * grid has finished and its writes are visible. */
 __device__ __forceinline__ void allow_dependent_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+/* Bulk prefetch of [p, p + bytes) into L2 by the copy engine (no registers,
+ * nothing to wait for); p 16-byte aligned, bytes a multiple of 16. */
+__device__ __forceinline__ void l2_prefetch(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 /* 16-byte global -> shared copies that bypass the registers (and L1) */

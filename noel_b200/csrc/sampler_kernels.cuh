@@ -12,6 +12,13 @@ constexpr int kMainThreads = 256;
 constexpr int kEPT = 16;         // buffer entries per thread in compactions (cap <= 4096)
 constexpr int kWarmBins = 2048;  // warm-up histogram on the top 11 key bits
 constexpr int kExactThreads = 256;
+#ifndef NOEL_BLOCK_PREFETCH
+#define NOEL_BLOCK_PREFETCH 1
+#endif
+/* Chunks (NT * U vectors, 32 KB) of the block kernel's row kept prefetched
+ * into L2 ahead of the one being read: each chunk ends in a block barrier,
+ * so without them every chunk pays a full memory latency. */
+constexpr int kBlockPrefetch = NOEL_BLOCK_PREFETCH;
 
 struct RowOut {
     int id, n_topk, n_final, num_cands, flags;
@@ -121,6 +128,13 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
     const int row = blockIdx.x;
     const int V = a.vocab;
     const void *rowp = static_cast<const char *>(a.logits) + (size_t)row * (size_t)a.ld * F::ES;
+    const RowGeom g = row_geom<T>(rowp, V);
+    const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
+    auto prefetch_chunk = [&](int it) {
+        const int v0 = it * NT * U;
+        if (v0 < g.nvec) l2_prefetch(vbase + v0, (uint32_t)(min(g.nvec - v0, NT * U) * (int)sizeof(V8)));
+    };
+    if (tid < kBlockPrefetch) prefetch_chunk(tid);  // land while the history is built
 
     /* shared-memory carve-up */
     unsigned char *sp = smem;
@@ -160,8 +174,6 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
                              a.rep);
     __syncthreads();
 
-    const RowGeom g = row_geom<T>(rowp, V);
-
     /* running state */
     float gx = -INFINITY;
     uint32_t gid = 0xFFFFFFFFu;
@@ -190,7 +202,6 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
     __syncthreads();
 
     /* ---- vector body ---- */
-    const V8 *vbase = reinterpret_cast<const V8 *>(static_cast<const char *>(rowp) + (size_t)g.head * F::ES);
     const int per_iter = NT * U;
     const int iters = (g.nvec + per_iter - 1) / per_iter;
     const bool warm = (MODE == kTopK) && min(g.nvec, per_iter) * VEC >= 2 * a.kprime;
@@ -272,6 +283,7 @@ __global__ void __launch_bounds__(kMainThreads, 2) sample_rows_block_kernel(cons
     }
 
     for (int it = 0; it < iters; ++it) {
+        if (kBlockPrefetch > 0 && tid == 0) prefetch_chunk(it + kBlockPrefetch);
         float x[NE];
         uint32_t valid = 0u;
         {

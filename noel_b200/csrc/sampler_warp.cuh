@@ -69,32 +69,52 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
         h.val[i] = 0u;
     }
     __syncthreads();
+    constexpr int R = kHistBatch;
     const int bits = __ffs(h.cap) - 1;
     const int lane = threadIdx.x & 31;
-    for (int base = first; base < H; base += NT) {  // whole warps per round
-        const int i = base + (int)threadIdx.x;
-        const int gt = i < H ? hrow[i] : -1;
-        const bool in = i < H && gt >= id_off && gt - id_off < V;  // sampler.c:95 (ids of this shard)
-        const uint32_t t = in ? (uint32_t)(gt - id_off) : 0xFFFFFFFFu;
-        /* lanes holding the same id insert it once, with their number (a
-         * skewed window repeats a few ids in most lanes) */
-        const uint32_t same = __match_any_sync(kFull, t);
-        if (!in || lane != __ffs(same) - 1) continue;
-        atomicOr(&h.blk[t >> 8], 1u << ((t >> 3) & 31));
-        uint32_t p = bits ? (hs_hash(t) >> (32 - bits)) : 0u;
-        for (int probe = 0; probe < h.cap; ++probe) {
-            const uint32_t prev = atomicCAS(&h.key[p], 0u, t + 1u);
-            if (prev == 0u || prev == t + 1u) {
-                atomicAdd(&h.val[p], (uint32_t)__popc(same));
-                break;
+    for (int b0 = first; b0 < H; b0 += NT * R) {  // R rounds of whole warps, their loads issued together
+        int gv[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = b0 + r * NT + (int)threadIdx.x;
+            gv[r] = i < H ? hrow[i] : -1;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = b0 + r * NT + (int)threadIdx.x;
+            const int gt = gv[r];
+            const bool in = i < H && gt >= id_off && gt - id_off < V;  // sampler.c:95 (ids of this shard)
+            const uint32_t t = in ? (uint32_t)(gt - id_off) : 0xFFFFFFFFu;
+            /* lanes holding the same id insert it once, with their number (a
+             * skewed window repeats a few ids in most lanes) */
+            const uint32_t same = __match_any_sync(kFull, t);
+            if (!in || lane != __ffs(same) - 1) continue;
+            atomicOr(&h.blk[t >> 8], 1u << ((t >> 3) & 31));
+            uint32_t p = bits ? (hs_hash(t) >> (32 - bits)) : 0u;
+            for (int probe = 0; probe < h.cap; ++probe) {
+                const uint32_t prev = atomicCAS(&h.key[p], 0u, t + 1u);
+                if (prev == 0u || prev == t + 1u) {
+                    atomicAdd(&h.val[p], (uint32_t)__popc(same));
+                    break;
+                }
+                p = (p + 1) & (uint32_t)(h.cap - 1);
             }
-            p = (p + 1) & (uint32_t)(h.cap - 1);
         }
     }
     __syncthreads();
-    for (int s = threadIdx.x; s < h.cap; s += NT) {
-        const uint32_t k = h.key[s];
-        if (k) h.val[s] = __float_as_uint(apply_penalty(Fmt<T>::scalar(rowp, (int)(k - 1u)), h.val[s], rep));
+    for (int s0 = threadIdx.x; s0 < h.cap; s0 += NT * R) {  // R logits loaded together
+        float xs[R];
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            const int s = s0 + k * NT;
+            const uint32_t key = s < h.cap ? h.key[s] : 0u;
+            xs[k] = key ? Fmt<T>::scalar(rowp, (int)(key - 1u)) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            const int s = s0 + k * NT;
+            if (s < h.cap && h.key[s]) h.val[s] = __float_as_uint(apply_penalty(xs[k], h.val[s], rep));
+        }
     }
     __syncthreads();
 }
