@@ -162,7 +162,12 @@ __device__ __forceinline__ void shard_write(const SampleArgs &a, int row, int id
 
 /* sampler.c:96-100 applied c times (one per occurrence in the window) */
 __device__ __forceinline__ float apply_penalty(float x, uint32_t c, float rep) {
-    for (uint32_t i = 0; i < c; ++i) x = (x > 0.0f) ? __fdiv_rn(x, rep) : __fmul_rn(x, rep);
+    /* the sign never changes (a positive value stays positive, zero stays
+     * zero), so the branch of sampler.c:97-100 is taken once */
+    if (x > 0.0f)
+        for (uint32_t i = 0; i < c; ++i) x = __fdiv_rn(x, rep);
+    else
+        for (uint32_t i = 0; i < c; ++i) x = __fmul_rn(x, rep);
     return x;
 }
 
@@ -328,10 +333,7 @@ __device__ void build_history(const HistView &h, const int32_t *hrow, int first,
             const int g = gv[r];
             const bool in = i < H && g >= id_off && g - id_off < V;  // sampler.c:95 (ids of this shard)
             const int t = g - id_off;
-            const uint32_t wd = in ? (uint32_t)(t >> 5) : 0xFFFFFFFFu;
-            const uint32_t grp = __match_any_sync(0xFFFFFFFFu, wd);
-            const uint32_t bits = __reduce_or_sync(grp, in ? 1u << (t & 31) : 0u);
-            if (in && (int)(threadIdx.x & 31) == __ffs(grp) - 1) atomicOr(&h.bm[wd], bits);
+            if (in) atomicOr(&h.bm[t >> 5], 1u << (t & 31));
         }
     }
     __syncthreads();
@@ -366,12 +368,9 @@ __device__ void build_history(const HistView &h, const int32_t *hrow, int first,
             const int i = b0 + r * NT + (int)threadIdx.x;
             const int g = gv[r];
             const bool in = i < H && g >= id_off && g - id_off < V;
-            const uint32_t same = __match_any_sync(0xFFFFFFFFu, in ? (uint32_t)(g - id_off) : 0xFFFFFFFFu);
-            /* lanes holding the same id count it once (a skewed window
-             * repeats a few ids in most lanes) */
-            if (in && (int)(threadIdx.x & 31) == __ffs(same) - 1) {
+            if (in) {
                 const int rk = hist_rank(h, g - id_off);
-                const uint32_t before = atomicAdd(&h.cnt[rk], (uint32_t)__popc(same));
+                const uint32_t before = atomicAdd(&h.cnt[rk], 1u);
                 if (h.idr && before == 0u) h.idr[rk] = (uint32_t)(g - id_off);  // the first count names the rank
             }
         }

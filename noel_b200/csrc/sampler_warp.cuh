@@ -71,7 +71,6 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
     __syncthreads();
     constexpr int R = kHistBatch;
     const int bits = __ffs(h.cap) - 1;
-    const int lane = threadIdx.x & 31;
     for (int b0 = first; b0 < H; b0 += NT * R) {  // R rounds of whole warps, their loads issued together
         int gv[R];
 #pragma unroll
@@ -84,17 +83,14 @@ __device__ void hs_build(const HistSet &h, const int32_t *hrow, int first, int H
             const int i = b0 + r * NT + (int)threadIdx.x;
             const int gt = gv[r];
             const bool in = i < H && gt >= id_off && gt - id_off < V;  // sampler.c:95 (ids of this shard)
-            const uint32_t t = in ? (uint32_t)(gt - id_off) : 0xFFFFFFFFu;
-            /* lanes holding the same id insert it once, with their number (a
-             * skewed window repeats a few ids in most lanes) */
-            const uint32_t same = __match_any_sync(kFull, t);
-            if (!in || lane != __ffs(same) - 1) continue;
+            if (!in) continue;
+            const uint32_t t = (uint32_t)(gt - id_off);
             atomicOr(&h.blk[t >> 8], 1u << ((t >> 3) & 31));
             uint32_t p = bits ? (hs_hash(t) >> (32 - bits)) : 0u;
             for (int probe = 0; probe < h.cap; ++probe) {
                 const uint32_t prev = atomicCAS(&h.key[p], 0u, t + 1u);
-                if (prev == 0u || prev == t + 1u) {
-                    atomicAdd(&h.val[p], (uint32_t)__popc(same));
+                if (prev == 0u || prev == t + 1u) {  // claimed, or the id's slot already
+                    atomicAdd(&h.val[p], 1u);
                     break;
                 }
                 p = (p + 1) & (uint32_t)(h.cap - 1);
