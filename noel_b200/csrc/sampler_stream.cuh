@@ -422,15 +422,14 @@ __device__ void hs_build_warp(const HistSet &h, const int32_t *hrow, int first, 
             const int i = b0 + u * 32 + lane;
             const int gt = gts[u];
             const bool in = i < H && gt >= id_off && gt - id_off < V;  // sampler.c:95
-            const uint32_t t = in ? (uint32_t)(gt - id_off) : 0xFFFFFFFFu;
-            const uint32_t same = __match_any_sync(kFull, t);
-            if (in && lane == __ffs(same) - 1) {
+            if (in) {  // lanes with the same id: one claims the slot, every lane counts
+                const uint32_t t = (uint32_t)(gt - id_off);
                 atomicOr(&h.blk[t >> 8], 1u << ((t >> 3) & 31));
                 uint32_t p = bits ? (hs_hash(t) >> (32 - bits)) : 0u;
                 for (int probe = 0; probe < h.cap; ++probe) {
                     const uint32_t prev = atomicCAS(&h.key[p], 0u, t + 1u);
                     if (prev == 0u || prev == t + 1u) {
-                        atomicAdd(&h.val[p], (uint32_t)__popc(same));
+                        atomicAdd(&h.val[p], 1u);
                         break;
                     }
                     p = (p + 1) & (uint32_t)(h.cap - 1);
