@@ -63,10 +63,21 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def profile_traffic(workload: str):
-    """DRAM bytes per launch of the single-pass kernel from the committed ncu
-    summary (line 'traffic_bytes_per_launch: N'), or None."""
-    p = os.path.join(ROOT, "profiles", f"sample_rows_kernel_{workload}.md")
+def main_kernel(w) -> str:
+    """The kernel that samples the workload's rows: the streaming kernel for
+    full lists (top-k off), the block kernel for top-k above 120, else the
+    one-CTA-per-row kernel (greedy and top-k up to 120)."""
+    if w.temperature > 1e-4 and w.top_k <= 0:
+        return "stream_rows_kernel"
+    if w.temperature > 1e-4 and w.top_k > 120:
+        return "sample_rows_block_kernel"
+    return "sample_rows_kernel"
+
+
+def profile_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch of the workload's main kernel from the committed
+    ncu summary (line 'traffic_bytes_per_launch: N'), or None."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -356,7 +367,7 @@ def run_ours(args):
     peak, peak_kind = measured_peak()
     bytes_per_launch = w.bytes_per_row() * B
     achieved = bytes_per_launch / (k_ms / 1e3) / 1e9
-    traffic = profile_traffic(w.name)
+    traffic = profile_traffic(main_kernel(w), w.name)
 
     # ---- end to end through the host-buffer C entry point ----
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
@@ -423,7 +434,7 @@ def run_ours(args):
             "config": workload_config(w, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "sample_rows_kernel", "kernel_ms": k_ms,
+                         "kernel": main_kernel(w), "kernel_ms": k_ms,
                          "bytes_per_launch": bytes_per_launch, "peak_source": f"{peak_kind} hbm_gbs"},
             "cpu_baseline": cpu,
             "parity": parity,
