@@ -36,6 +36,7 @@
 namespace noel {
 
 constexpr int kRowWarps = 4;  // warps streaming one row
+
 constexpr int kRowThreads = 32 * kRowWarps;
 constexpr int kWarpBins = 512;    // per level of the warm-up histogram (9 key bits)
 
@@ -240,6 +241,7 @@ struct RowShared {
     int wfill[kRowWarps];
     int next;                               // next batch to stream (queued modes)
     int w[kRowWarps + 1];
+    uint32_t wmax[kRowWarps];               // each warp's largest raw sample key (warm-up)
     float gx[kRowWarps];
     uint32_t gid[kRowWarps];
 };
@@ -514,10 +516,10 @@ __device__ __forceinline__ int warm_vec(int nvec, int warp, int u, int lane) {
  * lane) of each warp's queue holds the vector warm_vec names): the smallest
  * raw lane maximum of a warp has 32 raw elements above it and becomes the
  * warp's own threshold (an exclusion threshold checked at the row end, so it
- * needs no proof); the second largest of those bounds a two-level histogram
- * (9 key bits, then the next 9 inside the chosen bin) of the larger sample
- * elements, penalised, whose bin holding the r-th largest (r = warm_rank)
- * gives the row's starting filter.  With r < K' the filter is a bet, not a
+ * needs no proof); the second largest of those, lo_key, bounds a histogram
+ * of the larger sample elements, penalised, in 512 bins over [lo_key, the
+ * sample's largest raw key], and the floor of the bin holding the r-th
+ * largest (r = warm_rank) becomes the row's starting filter.  With r < K' the filter is a bet, not a
  * proof: it drops elements below it, and the row end sends the row to the
  * two-pass kernel when fewer than K' elements passed it.  The penalty only
  * lowers values, so only elements whose raw value reaches the histogram are
@@ -548,6 +550,10 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         tau_w = (unsigned long long)ord_key(t0) << 32;  // 32 of this warp's raw elements beat it
         if (lane == 0) rs.taus[warp] = tau_w;
     }
+    {
+        const float wm = warp_max_f(lmax);
+        if (lane == 0) rs.wmax[warp] = wm > -INFINITY ? ord_key(wm) : 0u;
+    }
     __syncthreads();
     unsigned long long t1 = 0ull, t2 = 0ull;
 #pragma unroll
@@ -561,6 +567,14 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
         }
     }
     const uint32_t lo_key = (uint32_t)(t2 >> 32);
+    /* 512 bins over the sample's key range [lo_key, largest raw key] (the
+     * penalty only lowers keys, so a penalised key above lo_key stays in it) */
+    uint32_t hi_key = 0u;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) hi_key = max(hi_key, rs.wmax[w]);
+    const uint32_t span = hi_key > lo_key ? hi_key - lo_key : 0u;
+    const int shift = span < (uint32_t)kWarpBins ? 0 : (32 - __clz((int)span)) - 9;
+    auto bin1 = [&](uint32_t key) -> uint32_t { return min((uint32_t)(kWarpBins - 1), (key - lo_key) >> shift); };
     /* The elements whose raw value reaches a floor form a bitmask; one
      * compact loop takes each one's value back from this warp's queue (which
      * still holds the batch) and its penalised value from the table (the
@@ -588,7 +602,7 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
     if (UX > 1) {
         for (uint64_t m = reach(lo_key); m; m &= m - 1) {
             const float xv = value(__ffsll((long long)m) - 1);
-            if (ord_key(xv) >= lo_key) atomicAdd(&L.area[ord_key(xv) >> 23], 1u);
+            if (ord_key(xv) >= lo_key) atomicAdd(&L.area[bin1(ord_key(xv))], 1u);
         }
     } else {
         if (a.penalty) {  // only what reaches the histogram needs its penalised value
@@ -606,38 +620,15 @@ __device__ __forceinline__ unsigned long long row_warmup(const SampleArgs &a, in
 #pragma unroll
         for (int e = 0; e < NE; ++e) {
             const float xv = xw[e];
-            if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key) atomicAdd(&L.area[ord_key(xv) >> 23], 1u);
+            if (xv == xv && xv > -INFINITY && ord_key(xv) >= lo_key) atomicAdd(&L.area[bin1(ord_key(xv))], 1u);
         }
     }
     __syncthreads();
     int need;
     const int wb1 = block_find_bin_desc<NT>(L.area, a.warm_rank > 0 ? a.warm_rank : a.kprime, rs.w, rs.res, &need);
-    if (wb1 >= 0) {
-        uint32_t *h2 = L.area + kWarpBins;
-        for (int i = tid; i < kWarpBins; i += NT) h2[i] = 0u;
-        __syncthreads();
-        if (UX > 1) {
-            for (uint64_t m = reach((uint32_t)wb1 << 23); m; m &= m - 1) {
-                const float xv = value(__ffsll((long long)m) - 1);
-                if (xv == xv && (int)(ord_key(xv) >> 23) == wb1) atomicAdd(&h2[(ord_key(xv) >> 14) & (kWarpBins - 1)], 1u);
-            }
-        } else {
-#pragma unroll
-            for (int e = 0; e < NE; ++e) {
-                const float xv = xw[e];
-                if (xv == xv && xv > -INFINITY && (int)(ord_key(xv) >> 23) == wb1)
-                    atomicAdd(&h2[(ord_key(xv) >> 14) & (kWarpBins - 1)], 1u);
-            }
-        }
-        __syncthreads();
-        int need2;
-        const int wb2 = block_find_bin_desc<NT>(h2, need, rs.w, rs.res, &need2);
-        if (tid == 0 && wb2 >= 0) {
-            const uint32_t key = ((uint32_t)wb1 << 23) | ((uint32_t)wb2 << 14);
-            rs.tsh = (unsigned long long)key << 32;  // r sample elements reach it
-        }
-        __syncthreads();
-    }
+    if (tid == 0 && wb1 >= 0)  // the bin's floor: r sample elements reach it
+        rs.tsh = (unsigned long long)(lo_key + ((uint32_t)wb1 << shift)) << 32;
+    __syncthreads();
     return tau_w;
 }
 
